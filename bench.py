@@ -1,0 +1,481 @@
+"""Benchmark of the ConvRot INT8 linear hot path on B200.
+
+Metric: "ConvRot int8 linear TOPS @M=2048,K=1280,N=10240;
+rotate+quant HBM GB/s".  One step is one INT8 ConvRot linear forward over one
+batch: rotate+quantize bf16 x [2048,1280] -> int8, then the tcgen05 int8 GEMM
+against the pre-rotated int8 weight [10240,1280] with the dequant epilogue
+fused -> bf16 [2048,10240] (the SDXL GEGLU up-projection shape, config C3/W1).
+``value`` = 2*M*N*K ops per step x steps x ranks / the device time of the
+timed region (max over ranks), in TOPS; inputs resident in HBM, six rotating
+buffer sets (x, weight, scales, output: 378 MB in all, three times the 126 MB
+L2) so no step reads the L2-resident leftovers of the previous one.  The
+timed steps are replayed from CUDA graphs of the same launches.
+
+Also reported on the same line:
+* ``roofline``: the GEMM kernel alone (its average launch time by CUDA
+  events), achieved int8 TOPS against the int8 dense peak (2x the measured
+  bf16 cuBLAS burst of MEASURED_PEAKS.json), with the DRAM traffic of one
+  launch from the committed ncu summary;
+* ``rotate_quant``: the rotate+quantize kernel at config C5 (x [65536,4096],
+  3*M*K + 4*M = 805.6 MB per launch) in HBM GB/s against the measured copy
+  bandwidth -- the metric's second half;
+* ``e2e``: the same step through the public API ``xpu_kernels.linear`` with x
+  copied from pinned host memory and the bf16 result copied back each step;
+* ``cpu_baseline``: the CPU oracle (the reference path restated in numpy,
+  float64 BLAS for the exact int8 GEMM) on a row sample of the workload.
+
+``--impl reference`` times the reference's CPU path (the oracle port: the
+reference's own library is SYCL for Intel GPUs and does not build here) on
+the host cores, on the same metric and unit.
+
+Multi-GPU (torchrun): every rank runs its own 2048-row batch against a
+replicated weight (M-sharding, no collective on the data path): "scaling":
+"weak".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "oko-xpu-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+M, K, N = 2048, 1280, 10240
+OPS = 2.0 * M * N * K
+METRIC = "ConvRot int8 linear TOPS @M=2048,K=1280,N=10240; rotate+quant HBM GB/s"
+NSETS = 6
+C5_M, C5_K = 65536, 4096
+C5_BYTES = 3 * C5_M * C5_K + 4 * C5_M
+WORKLOAD = ("linear(x bf16 [2048,1280]) -> rotate+quantize -> tcgen05 int8 GEMM with fused "
+            "dequant -> bf16 [2048,10240] (config C3 W1, SDXL GEGLU up-projection)")
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _committed_traffic():
+    """DRAM bytes per GEMM launch from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "gemm_i8_dequant_C3W1.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU arms
+
+def _cpu_inputs(rows, seed=2):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    return xb, wb
+
+
+def cpu_oracle_rate(rows: int, budget_s: float):
+    """TOPS of the CPU oracle's forward on `rows` rows of the workload, repeated
+    for about `budget_s` seconds (the weight is prepared once, untimed)."""
+    from oracle import convrot_oracle as O
+    xb, wb = _cpu_inputs(rows)
+    w8, ws = O.prepare_weight(wb)
+    O.linear(xb[:8], w8, ws)  # warm the BLAS threads
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.linear(xb, w8, ws)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return 2.0 * rows * N * K * reps / el / 1e12, reps, el
+
+
+def run_reference(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rows = 128
+    from oracle import convrot_oracle as O
+    xb, wb = _cpu_inputs(rows)
+    w8, wsc = O.prepare_weight(wb)
+    for _ in range(max(1, args.warmup)):
+        O.linear(xb, w8, wsc)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.linear(xb, w8, wsc)
+    el = time.perf_counter() - t0
+    value = 2.0 * rows * N * K * args.steps / el / 1e12
+    sample = (f"{rows} of the 2048 rows per step (same K, N, weight); the CPU oracle "
+              f"(numpy restatement of the reference path, float64 BLAS for the exact "
+              f"int8 GEMM)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,1) x, N(0,0.02) W)",
+        "config": {"workload": WORKLOAD, "rows_per_step": rows, "M": M, "K": K, "N": N},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference's device library is SYCL for Intel Xe2 and cannot be built or "
+                 "run here; its CPU path is timed through the oracle port"),
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def run_gpu(args):
+    import xpu_kernels
+    from xpu_kernels.int8 import _lib as L
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    lib = L._lib()
+    stream = torch.cuda.current_stream(dev)
+
+    # inputs: six buffer sets, each its own x, weight, scales and output
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = []
+    for i in range(NSETS):
+        x = torch.randn(M, K, generator=g, device=dev)
+        x[:, :13] *= 10  # 1 % outlier channels, as config C2 specifies
+        x = x.to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w8, wsc = xpu_kernels.prepare_weight(w)
+        bias = torch.randn(N, generator=g, device=dev) * 0.01
+        sets.append(dict(x=x, w8=w8, ws=wsc, bias=bias,
+                         out=torch.empty(M, N, dtype=torch.bfloat16, device=dev),
+                         xq=torch.empty(M, K, dtype=torch.int8, device=dev),
+                         xs=torch.empty(M, dtype=torch.float32, device=dev)))
+    sptr = L._stream(dev)
+
+    def step(s):
+        rc = lib.xpuint8_linear_stream(sptr, L._ptr(s["x"]), L._ptr(s["w8"]), L._ptr(s["ws"]),
+                                       L._ptr(s["bias"]), L._ptr(s["out"]), L._ptr(s["xq"]),
+                                       L._ptr(s["xs"]), M, N, K, 0)
+        if rc != 0:
+            raise RuntimeError(lib.xpuint8_last_error())
+
+    # correctness guard on the bench's own data: sampled rows against the oracle
+    step(sets[0])
+    torch.cuda.synchronize()
+    if rank == 0:
+        from oracle import convrot_oracle as O
+        rows = torch.arange(0, M, 341, device=dev)
+        xb = sets[0]["x"][rows].cpu().view(torch.int16).numpy().view(np.uint16)
+        ref = O.linear(xb, sets[0]["w8"].cpu().numpy(), sets[0]["ws"].cpu().numpy(),
+                       sets[0]["bias"].cpu().numpy())
+        got = sets[0]["out"][rows].cpu().view(torch.int16).numpy().view(np.uint16)
+        if not np.array_equal(got, ref):
+            raise RuntimeError("bench output differs from the oracle on sampled rows")
+
+    # CUDA graphs of the step over the buffer sets (capture on a side stream)
+    per_graph = NSETS * 10
+    capture_stream = torch.cuda.Stream(dev)
+    capture_stream.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(capture_stream):
+        csptr = L._stream(dev)
+        with torch.cuda.graph(graph, stream=capture_stream):
+            for j in range(per_graph):
+                s = sets[j % NSETS]
+                rc = lib.xpuint8_linear_stream(csptr, L._ptr(s["x"]), L._ptr(s["w8"]),
+                                               L._ptr(s["ws"]), L._ptr(s["bias"]),
+                                               L._ptr(s["out"]), L._ptr(s["xq"]),
+                                               L._ptr(s["xs"]), M, N, K, 0)
+                if rc != 0:
+                    raise RuntimeError(lib.xpuint8_last_error())
+    stream.wait_stream(capture_stream)
+    torch.cuda.synchronize()
+
+    def run_steps(n):
+        full, rest = divmod(n, per_graph)
+        for _ in range(full):
+            graph.replay()
+        for j in range(rest):
+            step(sets[j % NSETS])
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    run_steps(max(3, args.warmup))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(stream)
+        run_steps(args.steps)
+        e1.record(stream)
+        e1.synchronize()
+        barrier()
+    t_ms = e0.elapsed_time(e1)
+    if ws > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([t_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    value = OPS * args.steps * ws / (t_ms * 1e-3) / 1e12
+    clocks = clk.summary()
+
+    # eager launches (no graph) for context
+    torch.cuda.synchronize()
+    n_eager = min(args.steps, 600)
+    e0.record(stream)
+    for j in range(n_eager):
+        step(sets[j % NSETS])
+    e1.record(stream)
+    e1.synchronize()
+    eager_ms = e0.elapsed_time(e1) / n_eager
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) x with 1% outlier channels x10, N(0,0.02) W, "
+                "random-init weights prepared with prepare_weight)",
+        "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "per_rank_rows": M,
+                   "parallelism": f"M-shard x{ws} (replicated weights, no collective)",
+                   "l2": f"{NSETS} rotating buffer sets, "
+                         f"{NSETS * (M * K * 3 + N * K + M * N * 2) / 1e6:.0f} MB > 126 MB L2",
+                   "timing": "CUDA-graph replay of the same launches; eager launches in "
+                             "eager_ms_per_step"},
+        "eager_ms_per_step": eager_ms,
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }
+
+    if rank == 0:
+        result.update(_rank0_extras(args, lib, L, dev, sets, stream))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    del graph
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+    return 0
+
+
+def _time_launches(fn, n, stream):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(n):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def _rank0_extras(args, lib, L, dev, sets, stream):
+    import xpu_kernels
+    peaks, src = _peaks()
+    sptr = L._stream(dev)
+    out = {}
+
+    # the GEMM alone: the dominant kernel (inputs already quantized)
+    for s in sets:
+        lib.xpuint8_convrot_quantize_stream(sptr, L._ptr(s["x"]), L._ptr(s["xq"]), L._ptr(s["xs"]),
+                                            M, K)
+
+    def gemm(i):
+        s = sets[i % NSETS]
+        lib.xpuint8_int_mm_dequant_stream(sptr, L._ptr(s["xq"]), L._ptr(s["w8"]), L._ptr(s["out"]),
+                                          L._ptr(s["xs"]), L._ptr(s["ws"]), L._ptr(s["bias"]),
+                                          M, N, K, 0, N)
+
+    for i in range(12):
+        gemm(i)
+    t_gemm = _time_launches(gemm, 300, stream)
+    achieved = OPS / (t_gemm * 1e-3) / 1e12
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    traffic = _committed_traffic()
+    out["roofline"] = {
+        "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+        "frac": achieved / int8_peak, "traffic": traffic,
+        "kernel": "gemm_i8_kernel<dequant> (tcgen05.mma.kind::i8 128x256x32, TMA, TMEM x2)",
+        "ms_per_launch": t_gemm,
+        "peak_source": (f"int8 dense = 2 x the {src} bf16 cuBLAS burst "
+                        f"({peaks['bf16_tflops']} TFLOP/s); unit is int8 TOPS"),
+        "algorithmic": "2*M*N*K = 53.69 GOP per launch",
+    }
+    # cuBLASLt int8 (torch._int_mm) on the same operands, as a library comparison
+    try:
+        def cublas(i):
+            s = sets[i % NSETS]
+            torch._int_mm(s["xq"], s["w8"].t())
+        for i in range(6):
+            cublas(i)
+        t_cub = _time_launches(cublas, 100, stream)
+        out["roofline"]["cublaslt_int_mm_tops"] = OPS / (t_cub * 1e-3) / 1e12
+    except Exception as exc:  # noqa: BLE001 - context only
+        out["roofline"]["cublaslt_int_mm_tops"] = f"unavailable: {exc}"
+
+    # rotate+quantize at config C5, the HBM-bound half of the metric
+    del_sets = []
+    try:
+        g = torch.Generator(device=dev).manual_seed(4)
+        big = []
+        for i in range(2):
+            x = torch.randn(C5_M, C5_K, generator=g, device=dev).to(torch.bfloat16)
+            big.append((x, torch.empty(C5_M, C5_K, dtype=torch.int8, device=dev),
+                        torch.empty(C5_M, dtype=torch.float32, device=dev)))
+        del_sets = big
+
+        def rq(i):
+            x, q, s = big[i % 2]
+            lib.xpuint8_convrot_quantize_stream(sptr, L._ptr(x), L._ptr(q), L._ptr(s), C5_M, C5_K)
+
+        for i in range(4):
+            rq(i)
+        t_rq = _time_launches(rq, 40, stream)
+        gbs = C5_BYTES / (t_rq * 1e-3) / 1e9
+        out["rotate_quant"] = {
+            "shape": "x bf16 [65536,4096] (config C5)", "ms_per_launch": t_rq, "gbs": gbs,
+            "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+            "algorithmic_bytes": C5_BYTES, "peak_source": f"{src} copy bandwidth",
+        }
+    finally:
+        del del_sets
+        torch.cuda.empty_cache()
+
+    # end to end through the public API with host buffers
+    x_host = [s["x"].cpu().pin_memory() for s in sets[:2]]
+    y_host = [torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    s0 = sets[0]
+
+    def e2e(i):
+        xd = x_host[i % 2].to(dev, non_blocking=True)
+        y = xpu_kernels.linear(xd, s0["w8"], s0["ws"], s0["bias"])
+        y_host[i % 2].copy_(y, non_blocking=True)
+
+    for i in range(3):
+        e2e(i)
+    n_e2e = 50
+    t_e2e = _time_launches(e2e, n_e2e, stream)
+    out["e2e"] = {"value": OPS / (t_e2e * 1e-3) / 1e12, "unit": "TOPS",
+                  "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                  "ms_per_step": t_e2e, "api": "xpu_kernels.linear (pinned host in/out)"}
+
+    # the CPU baseline: the oracle on a row sample
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rate, reps, el = cpu_oracle_rate(128, budget_s=float(os.environ.get("CPU_BASELINE_S", "10")))
+    out["cpu_baseline"] = {
+        "value": rate, "unit": "TOPS", "cores": cores, "kind": "port",
+        "sample": (f"128 of the 2048 rows x {reps} repetitions ({el:.1f} s): the CPU oracle "
+                   f"(numpy restatement of the reference path, float64 BLAS GEMM)")}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,171 @@
+/* libxpuint8 for NVIDIA B200 (sm_100a): fused ConvRot INT8 primitives.
+ *
+ * A drop-in for the reference library's C ABI (okolenmi/oko-xpu-kernels,
+ * include/xpu_kernels/convrot.h): the same symbols, argument meanings and
+ * return codes, implemented with hand-written CUDA kernels.  Each declaration
+ * below cites the reference declaration it replaces.  The entries after the
+ * marked line are new: the reference obtained the GEMM from torch._int_mm and
+ * the row quantizer from Triton, so it has no C symbol for them.
+ *
+ * Pointers are caller-owned device pointers (16-byte aligned); nothing is
+ * allocated per call.  Scales and bias are fp32; activations and outputs bf16.
+ *
+ * Streams: `stream` is a cudaStream_t passed as `const void *` (the
+ * reference's `const void *sycl_queue`).  NULL selects the legacy default
+ * stream (torch's default stream has handle 0), where the reference returned
+ * an error for a null queue.  `_stream` entries enqueue asynchronously and
+ * never synchronise; the entries without a stream run on the legacy default
+ * stream and block until the work is done.
+ *
+ * Return codes: 0 ok; 1 no usable device; 2 bad size, null pointer or
+ * misalignment; 3 K (or the FFN inner width) not a multiple of 256; 4
+ * unsupported group count (K > 32768); 5 kernel launch failure; 6 bad
+ * activation id.  The message is in xpuint8_last_error() (per thread).
+ */
+#ifndef XPU_INT8_H
+#define XPU_INT8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Checks that a compute capability 10.0 device is present.
+ * Replaces convrot.h:30 xpuint8_init. */
+int xpuint8_init(void);
+
+/* Name of the current device, or NULL without one.
+ * Replaces convrot.h:33 xpuint8_device_name. */
+const char *xpuint8_device_name(void);
+
+/* The ConvRot group size, 256.  Replaces convrot.h:37 xpuint8_convrot_groupsize. */
+int xpuint8_convrot_groupsize(void);
+
+/* Rotate + quantize: x bf16 [M,K] -> q int8 [M,K] + scale fp32 [M].
+ * Replaces convrot.h:41-42 xpuint8_convrot_quantize and :46-47 _stream. */
+int xpuint8_convrot_quantize(const void *x, int8_t *q, float *scale, int64_t M, int64_t K);
+int xpuint8_convrot_quantize_stream(const void *stream, const void *x, int8_t *q, float *scale,
+                                    int64_t M, int64_t K);
+
+/* Activation fused before rotation and quantization: 1 GELU-tanh [M,K];
+ * 2 SwiGLU [M,2K] as [gate, up]; 3 situ [M,2K] as [hidden, gate]; 4 GEGLU
+ * (erf) [M,2K] as [hidden, gate]; 5 GELU-erf [M,K].  Output int8 [M,K].
+ * Replaces convrot.h:58-62 xpuint8_convrot_quantize_act and _stream. */
+int xpuint8_convrot_quantize_act(const void *x, int8_t *q, float *scale, int64_t M, int64_t K,
+                                 int32_t activation);
+int xpuint8_convrot_quantize_act_stream(const void *stream, const void *x, int8_t *q,
+                                        float *scale, int64_t M, int64_t K, int32_t activation);
+
+/* int8 [N,K] + fp32 [N] -> bf16 [N,K]: bf16(w8 * s) then the rotation undone.
+ * Replaces convrot.h:67-70 xpuint8_dequant_weight and _stream. */
+int xpuint8_dequant_weight(const void *w8, const float *w_scale, void *out, int64_t N,
+                           int64_t K);
+int xpuint8_dequant_weight_stream(const void *stream, const void *w8, const float *w_scale,
+                                  void *out, int64_t N, int64_t K);
+
+/* Rotation only, bf16 [M,K] -> bf16 [M,K].
+ * Replaces convrot.h:72-74 xpuint8_convrot_rotate_bf16 and _stream. */
+int xpuint8_convrot_rotate_bf16(const void *x, void *xr, int64_t M, int64_t K);
+int xpuint8_convrot_rotate_bf16_stream(const void *stream, const void *x, void *xr, int64_t M,
+                                       int64_t K);
+
+/* out bf16 [M,N] = bf16(float(acc) * (w_scale[n] * x_scale[m]) + bias[n]);
+ * bias may be NULL; N % 16 == 0.
+ * Replaces convrot.h:78-85 xpuint8_dequant_epilogue and _stream. */
+int xpuint8_dequant_epilogue(const int32_t *acc, void *out, const float *x_scale,
+                             const float *w_scale, const float *bias, int64_t M, int64_t N);
+int xpuint8_dequant_epilogue_stream(const void *stream, const int32_t *acc, void *out,
+                                    const float *x_scale, const float *w_scale,
+                                    const float *bias, int64_t M, int64_t N);
+
+/* As above for a [M,N] column slice of a [M, acc_row_stride] accumulator.
+ * Replaces convrot.h:90-96 xpuint8_dequant_epilogue_slice and _stream. */
+int xpuint8_dequant_epilogue_slice(const int32_t *acc, void *out, const float *x_scale,
+                                   const float *w_scale, const float *bias, int64_t M, int64_t N,
+                                   int64_t acc_row_stride);
+int xpuint8_dequant_epilogue_slice_stream(const void *stream, const int32_t *acc, void *out,
+                                          const float *x_scale, const float *w_scale,
+                                          const float *bias, int64_t M, int64_t N,
+                                          int64_t acc_row_stride);
+
+/* Dequant + activation (3 situ, 4 GEGLU, 5 GELU-erf) + rotate + quantize of an
+ * up-projection accumulator: acc int32 [M,2K] (paired) or [M,K]; w_scale
+ * [2K] or [K]; q int8 [M,K] + scale [M].
+ * Replaces convrot.h:106-112 xpuint8_dequant_act_quantize and _stream. */
+int xpuint8_dequant_act_quantize(const void *acc, int8_t *q, float *scale, const float *x_scale,
+                                 const float *w_scale, int64_t M, int64_t K, int32_t activation);
+int xpuint8_dequant_act_quantize_stream(const void *stream, const void *acc, int8_t *q,
+                                        float *scale, const float *x_scale,
+                                        const float *w_scale, int64_t M, int64_t K,
+                                        int32_t activation);
+
+/* Message of the last failure on this thread.  Replaces convrot.h:114. */
+const char *xpuint8_last_error(void);
+
+/* ---------------- new entries (no C symbol in the reference) ---------------- */
+
+/* int8 GEMM on the tensor cores, exact int32 result c [M,N] (row stride ldc).
+ * layout 0: a [M,K], b [N,K] -> a @ b^T  (torch._int_mm(a, b.t()), ops.py:587,634,714,716)
+ * layout 1: a [M,K], b [K,N] -> a @ b    (torch._int_mm(a, b), ops.py:371)
+ * layout 2: a [K,M], b [K,N] -> a^T @ b  (the int8 weight gradient)
+ * Row lengths of a and b must be multiples of 16 bytes; N % 16 == 0. */
+int xpuint8_int_mm_stream(const void *stream, const int8_t *a, const int8_t *b, int32_t *c,
+                          int64_t M, int64_t N, int64_t K, int32_t layout, int64_t ldc);
+
+/* The GEMM with the dequant epilogue fused into the accumulator drain:
+ * out bf16 [M,N] = bf16(float(a*b) * (col_scale[n] * row_scale[m]) + bias[n]).
+ * col_scale NULL means 1; bias may be NULL.  Replaces the pair
+ * torch._int_mm + xpuint8_dequant_epilogue (ops.py:634 + :479-497). */
+int xpuint8_int_mm_dequant_stream(const void *stream, const int8_t *a, const int8_t *b,
+                                  void *out, const float *row_scale, const float *col_scale,
+                                  const float *bias, int64_t M, int64_t N, int64_t K,
+                                  int32_t layout, int64_t ldo);
+
+/* Up-projection GEMM with the GEGLU epilogue: up_w8 [2*inner, K] as [hidden;
+ * gate], up_scale [2*inner]; y bf16 [M, inner] = bf16(h * bf16(gelu_erf(g)))
+ * with h, g the bf16 dequants.  Replaces torch._int_mm + the dequant and
+ * GEGLU of xpuint8_dequant_act_quantize (ops.py:714-715). */
+int xpuint8_int_mm_geglu_stream(const void *stream, const int8_t *a, const int8_t *up_w8,
+                                void *y, const float *x_scale, const float *up_scale, int64_t M,
+                                int64_t inner, int64_t K);
+
+/* The whole INT8 linear: rotate+quantize x (activation 0..5 as in
+ * _quantize_act), then the GEMM with the fused dequant epilogue.  xq int8
+ * [M,K] and xs fp32 [M] are caller-provided scratch.  Replaces
+ * python/xpu_kernels/int8/ops.py:591-646 (linear) in one C call. */
+int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
+                          const float *w_scale, const float *bias, void *out, int8_t *xq,
+                          float *xs, int64_t M, int64_t N, int64_t K, int32_t activation);
+
+/* The fused FFN down(act(up(x))) (ops.py:649-719) in one C call; activation 3
+ * situ, 4 GEGLU (fused into the up-projection's epilogue), 5 GELU-erf.
+ * `workspace` holds xpuint8_ffn_workspace_bytes(M, K, inner, activation)
+ * bytes of caller-provided scratch. */
+int64_t xpuint8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t inner, int32_t activation);
+int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
+                       const float *up_scale, const int8_t *down_w8, const float *down_scale,
+                       const float *down_bias, void *out, void *workspace, int64_t M, int64_t K,
+                       int64_t inner, int32_t activation);
+
+/* Per-row int8 quantization without rotation (the gradient quantizer):
+ * scale = max(amax/127, 1e-30), q = rint(x / scale).  With col_scale non-NULL
+ * the input is bf16(x * bf16(col_scale[k])) (linear_dx_int8's column scale).
+ * Replaces the Triton kernel triton/quantize.py:63-126 and the chain
+ * quantize_row_torch (ops.py:320-330).  K % 8 == 0. */
+int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *col_scale,
+                                int8_t *q, float *scale, int64_t M, int64_t K);
+
+/* Column quantization of g = dy[m,n] * x_scale[m] over m, for the int8 weight
+ * gradient: gq int8 [M,N], tg fp32 [N].  N % 16 == 0. */
+int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_scale, int8_t *gq,
+                            float *tg, int64_t M, int64_t N);
+
+/* The device fault word of the GEMM's bounded waits (0 = none), read with a
+ * device synchronisation; reset != 0 clears it. */
+int xpuint8_fault_status(int32_t reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XPU_INT8_H */

@@ -1,0 +1,499 @@
+// The C ABI of libxpuint8 (include/xpu_kernels/convrot.h): argument checks,
+// return codes, error text, and dispatch to the sm_100a kernels.
+//
+// Return codes follow the reference library (src/xpuint8.cpp:730-1081):
+//   0 ok; 1 no usable device; 2 bad size / pointer / alignment; 3 K not a
+//   multiple of 256; 4 unsupported group count; 5 launch failure; 6 bad
+//   activation id.
+// Stream semantics: `stream` is a cudaStream_t (the reference's `sycl_queue`
+// argument).  NULL is the legacy default stream -- torch's default stream has
+// handle 0 -- which is a deliberate difference from the reference, where a
+// null queue is an error.  `_stream` entries enqueue and return; the entries
+// without a stream run on the legacy default stream and wait for completion,
+// as the reference's blocking entries do.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+#include "xpu_kernels/convrot.h"
+
+namespace xpuint8 {
+
+namespace {
+thread_local std::string g_error;
+std::mutex g_init_mutex;
+int g_init_rc = -1;
+constexpr int kMaxDevices = 64;
+std::string g_names[kMaxDevices];
+int g_sms[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) return 0;
+    return d < kMaxDevices ? d : 0;
+}
+void fill_device(int d) {
+    std::call_once(g_dev_once[d], [d] {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, d) == cudaSuccess) {
+            g_names[d] = prop.name;
+            g_sms[d] = prop.multiProcessorCount;
+        } else {
+            g_sms[d] = 148;
+        }
+    });
+}
+}  // namespace
+
+void set_error(const std::string &msg) { g_error = msg; }
+
+int launch_status(const char *what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return 0;
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return 5;
+}
+
+int num_sms() {
+    const int d = current_device();
+    fill_device(d);
+    return g_sms[d] > 0 ? g_sms[d] : 148;
+}
+
+}  // namespace xpuint8
+
+using namespace xpuint8;
+
+namespace {
+
+cudaStream_t as_stream(const void *s) { return static_cast<cudaStream_t>(const_cast<void *>(s)); }
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_mk(int64_t M, int64_t K) {
+    if (M <= 0 || K <= 0) {
+        set_error("M and K must be positive");
+        return 2;
+    }
+    if (K % 256 != 0) {
+        set_error("K must be divisible by the ConvRot group size (256)");
+        return 3;
+    }
+    return 0;
+}
+
+int check_ptrs(std::initializer_list<const void *> ptrs) {
+    for (const void *p : ptrs) {
+        if (!p) {
+            set_error("a required pointer is null");
+            return 2;
+        }
+        if (!aligned16(p)) {
+            set_error("device pointers must be 16-byte aligned");
+            return 2;
+        }
+    }
+    return 0;
+}
+
+// the blocking entries: run on the legacy default stream and wait
+int finish_blocking(int rc, const char *what) {
+    if (rc != 0) return rc;
+    const cudaError_t e = cudaStreamSynchronize(0);
+    if (e != cudaSuccess) {
+        set_error(std::string(what) + ": " + cudaGetErrorString(e));
+        return 5;
+    }
+    return 0;
+}
+
+int convrot_quantize(cudaStream_t s, const void *x, int8_t *q, float *scale, int64_t M,
+                     int64_t K, int act) {
+    if (int rc = check_mk(M, K)) return rc;
+    if (act < 0 || act > 5) {
+        set_error("activation must be 1 (GELU-tanh), 2 (SwiGLU), 3 (situ), 4 (GEGLU) "
+                  "or 5 (GELU-erf)");
+        return 6;
+    }
+    if (int rc = check_ptrs({x, q, scale})) return rc;
+    return launch_rotate_rows(s, 0, act, x, nullptr, nullptr, q, scale, M, K);
+}
+
+int dequant_act_quantize(cudaStream_t s, const void *acc, int8_t *q, float *scale,
+                         const float *x_scale, const float *w_scale, int64_t M, int64_t K,
+                         int32_t act) {
+    if (int rc = check_mk(M, K)) return rc;
+    if (act != 3 && act != 4 && act != 5) {
+        set_error("dequant_act_quantize supports activation 3 (situ), 4 (GEGLU) or 5 (GELU-erf)");
+        return 6;
+    }
+    if (int rc = check_ptrs({acc, q, w_scale})) return rc;
+    if (!x_scale || !scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    return launch_rotate_rows(s, 1, act, acc, w_scale, x_scale, q, scale, M, K);
+}
+
+int rotate_bf16(cudaStream_t s, const void *x, void *xr, int64_t M, int64_t K) {
+    if (int rc = check_mk(M, K)) return rc;
+    if (int rc = check_ptrs({x, xr})) return rc;
+    return launch_rotate_rows(s, 2, 0, x, nullptr, nullptr, xr, nullptr, M, K);
+}
+
+int dequant_weight(cudaStream_t s, const void *w8, const float *w_scale, void *out, int64_t N,
+                   int64_t K) {
+    if (N <= 0 || K <= 0) {
+        set_error("N and K must be positive");
+        return 2;
+    }
+    if (K % 256 != 0) {
+        set_error("K must be divisible by the ConvRot group size (256)");
+        return 3;
+    }
+    if (int rc = check_ptrs({w8, out})) return rc;
+    if (!w_scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    return launch_rotate_rows(s, 3, 0, w8, w_scale, nullptr, out, nullptr, N, K);
+}
+
+int dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float *x_scale,
+                     const float *w_scale, const float *bias, int64_t M, int64_t N,
+                     int64_t stride, bool slice) {
+    if (M <= 0 || N <= 0 || N % 16 != 0 || stride < N) {
+        set_error(slice ? "M, N must be positive, N a multiple of 16, acc_row_stride >= N"
+                        : "M, N must be positive and N must be a multiple of 16");
+        return 2;
+    }
+    if (!acc || !out || !x_scale || !w_scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    if (!aligned16(out) || !aligned16(w_scale) || (bias && !aligned16(bias)) ||
+        (reinterpret_cast<uintptr_t>(acc) & 3u)) {
+        set_error("out, w_scale and bias must be 16-byte aligned");
+        return 2;
+    }
+    return launch_dequant_epilogue(s, acc, out, x_scale, w_scale, bias, M, N, stride);
+}
+
+// layout: 0 = a [M,K], b [N,K] (a @ b^T); 1 = a [M,K], b [K,N] (a @ b);
+//         2 = a [K,M], b [K,N] (a^T @ b)
+int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, void *out,
+                  const float *row_scale, const float *col_scale, const float *bias, int64_t M,
+                  int64_t N, int64_t K, int32_t layout, int64_t ldo) {
+    if (M <= 0 || N <= 0 || K <= 0) {
+        set_error("M, N and K must be positive");
+        return 2;
+    }
+    if (layout < 0 || layout > 2) {
+        set_error("layout must be 0 (a @ b.T), 1 (a @ b) or 2 (a.T @ b)");
+        return 2;
+    }
+    if (!a || !b || !out) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    if (ldo < N) {
+        set_error("the output row stride must be >= N");
+        return 2;
+    }
+    GemmCall c;
+    c.epilogue = epi;
+    c.a = a; c.b = b; c.out = out; c.ldo = ldo;
+    c.row_scale = row_scale; c.col_scale = col_scale; c.bias = bias;
+    c.M = M; c.N = N; c.K = K;
+    c.a_mn = layout == 2;
+    c.b_mn = layout >= 1;
+    c.lda = c.a_mn ? M : K;
+    c.ldb = c.b_mn ? N : K;
+    if ((c.lda % 16) || (c.ldb % 16) || !aligned16(a) || !aligned16(b)) {
+        set_error("int8 operands need 16-byte aligned bases and row lengths that are "
+                  "multiples of 16");
+        return 2;
+    }
+    return launch_gemm(s, c);
+}
+
+size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+struct FfnLayout {
+    size_t xq, xs, mid, q2, xs2, total;
+};
+FfnLayout ffn_layout(int64_t M, int64_t K, int64_t inner, int act) {
+    FfnLayout L{};
+    size_t off = 0;
+    L.xq = off; off += align256(static_cast<size_t>(M) * K);
+    L.xs = off; off += align256(static_cast<size_t>(M) * 4);
+    L.mid = off;
+    if (act == 4) off += align256(static_cast<size_t>(M) * inner * 2);        // y bf16
+    else off += align256(static_cast<size_t>(M) * inner * (act == 5 ? 4 : 8));  // int32 acc
+    L.q2 = off; off += align256(static_cast<size_t>(M) * inner);
+    L.xs2 = off; off += align256(static_cast<size_t>(M) * 4);
+    L.total = off;
+    return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int xpuint8_init(void) {
+    std::lock_guard<std::mutex> lock(g_init_mutex);
+    if (g_init_rc >= 0) return g_init_rc;
+    int n = 0;
+    const cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        set_error(std::string("no CUDA device: ") +
+                  (e != cudaSuccess ? cudaGetErrorString(e) : "device count is 0"));
+        g_init_rc = 1;
+        return 1;
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10 || prop.minor != 0) {
+        set_error("libxpuint8 is built for sm_100a (B200); the current device is not compute "
+                  "capability 10.0");
+        g_init_rc = 1;
+        return 1;
+    }
+    g_init_rc = 0;
+    return 0;
+}
+
+const char *xpuint8_device_name(void) {
+    if (xpuint8_init() != 0) return nullptr;
+    const int d = current_device();
+    fill_device(d);
+    return g_names[d].c_str();
+}
+
+int xpuint8_convrot_groupsize(void) { return 256; }
+
+const char *xpuint8_last_error(void) { return g_error.c_str(); }
+
+int xpuint8_convrot_quantize(const void *x, int8_t *q, float *scale, int64_t M, int64_t K) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(convrot_quantize(0, x, q, scale, M, K, 0), "convrot_quantize");
+}
+
+int xpuint8_convrot_quantize_stream(const void *stream, const void *x, int8_t *q, float *scale,
+                                    int64_t M, int64_t K) {
+    return convrot_quantize(as_stream(stream), x, q, scale, M, K, 0);
+}
+
+int xpuint8_convrot_quantize_act(const void *x, int8_t *q, float *scale, int64_t M, int64_t K,
+                                 int32_t activation) {
+    if (xpuint8_init() != 0) return 1;
+    if (activation < 1 || activation > 5) {
+        set_error("activation must be 1 (GELU-tanh), 2 (SwiGLU), 3 (situ), 4 (GEGLU) "
+                  "or 5 (GELU-erf)");
+        return 6;
+    }
+    return finish_blocking(convrot_quantize(0, x, q, scale, M, K, activation),
+                           "convrot_quantize_act");
+}
+
+int xpuint8_convrot_quantize_act_stream(const void *stream, const void *x, int8_t *q, float *scale,
+                                        int64_t M, int64_t K, int32_t activation) {
+    if (activation < 1 || activation > 5) {
+        set_error("activation must be 1 (GELU-tanh), 2 (SwiGLU), 3 (situ), 4 (GEGLU) "
+                  "or 5 (GELU-erf)");
+        return 6;
+    }
+    return convrot_quantize(as_stream(stream), x, q, scale, M, K, activation);
+}
+
+int xpuint8_dequant_weight(const void *w8, const float *w_scale, void *out, int64_t N, int64_t K) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(dequant_weight(0, w8, w_scale, out, N, K), "dequant_weight");
+}
+
+int xpuint8_dequant_weight_stream(const void *stream, const void *w8, const float *w_scale,
+                                  void *out, int64_t N, int64_t K) {
+    return dequant_weight(as_stream(stream), w8, w_scale, out, N, K);
+}
+
+int xpuint8_convrot_rotate_bf16(const void *x, void *xr, int64_t M, int64_t K) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(rotate_bf16(0, x, xr, M, K), "convrot_rotate_bf16");
+}
+
+int xpuint8_convrot_rotate_bf16_stream(const void *stream, const void *x, void *xr, int64_t M,
+                                       int64_t K) {
+    return rotate_bf16(as_stream(stream), x, xr, M, K);
+}
+
+int xpuint8_dequant_epilogue(const int32_t *acc, void *out, const float *x_scale,
+                             const float *w_scale, const float *bias, int64_t M, int64_t N) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(dequant_epilogue(0, acc, out, x_scale, w_scale, bias, M, N, N, false),
+                           "dequant_epilogue");
+}
+
+int xpuint8_dequant_epilogue_stream(const void *stream, const int32_t *acc, void *out,
+                                    const float *x_scale, const float *w_scale, const float *bias,
+                                    int64_t M, int64_t N) {
+    return dequant_epilogue(as_stream(stream), acc, out, x_scale, w_scale, bias, M, N, N, false);
+}
+
+int xpuint8_dequant_epilogue_slice(const int32_t *acc, void *out, const float *x_scale,
+                                   const float *w_scale, const float *bias, int64_t M, int64_t N,
+                                   int64_t acc_row_stride) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(dequant_epilogue(0, acc, out, x_scale, w_scale, bias, M, N,
+                                            acc_row_stride, true),
+                           "dequant_epilogue_slice");
+}
+
+int xpuint8_dequant_epilogue_slice_stream(const void *stream, const int32_t *acc, void *out,
+                                          const float *x_scale, const float *w_scale,
+                                          const float *bias, int64_t M, int64_t N,
+                                          int64_t acc_row_stride) {
+    return dequant_epilogue(as_stream(stream), acc, out, x_scale, w_scale, bias, M, N,
+                            acc_row_stride, true);
+}
+
+int xpuint8_dequant_act_quantize(const void *acc, int8_t *q, float *scale, const float *x_scale,
+                                 const float *w_scale, int64_t M, int64_t K, int32_t activation) {
+    if (xpuint8_init() != 0) return 1;
+    return finish_blocking(dequant_act_quantize(0, acc, q, scale, x_scale, w_scale, M, K, activation),
+                           "dequant_act_quantize");
+}
+
+int xpuint8_dequant_act_quantize_stream(const void *stream, const void *acc, int8_t *q,
+                                        float *scale, const float *x_scale, const float *w_scale,
+                                        int64_t M, int64_t K, int32_t activation) {
+    return dequant_act_quantize(as_stream(stream), acc, q, scale, x_scale, w_scale, M, K,
+                                activation);
+}
+
+// ---------------------------------------------------------------- new entries
+
+int xpuint8_int_mm_stream(const void *stream, const int8_t *a, const int8_t *b, int32_t *c,
+                          int64_t M, int64_t N, int64_t K, int32_t layout, int64_t ldc) {
+    return int_mm_common(as_stream(stream), kEpiRawI32, a, b, c, nullptr, nullptr, nullptr, M, N,
+                         K, layout, ldc);
+}
+
+int xpuint8_int_mm_dequant_stream(const void *stream, const int8_t *a, const int8_t *b, void *out,
+                                  const float *row_scale, const float *col_scale,
+                                  const float *bias, int64_t M, int64_t N, int64_t K,
+                                  int32_t layout, int64_t ldo) {
+    if (!row_scale) {
+        set_error("row_scale must not be null");
+        return 2;
+    }
+    return int_mm_common(as_stream(stream), kEpiDequantBf16, a, b, out, row_scale, col_scale, bias,
+                         M, N, K, layout, ldo);
+}
+
+int xpuint8_int_mm_geglu_stream(const void *stream, const int8_t *a, const int8_t *up_w8, void *y,
+                                const float *x_scale, const float *up_scale, int64_t M,
+                                int64_t inner, int64_t K) {
+    if (!x_scale || !up_scale) {
+        set_error("x_scale and up_scale must not be null");
+        return 2;
+    }
+    return int_mm_common(as_stream(stream), kEpiGegluBf16, a, up_w8, y, x_scale, up_scale, nullptr,
+                         M, inner, K, 0, inner);
+}
+
+int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
+                          const float *w_scale, const float *bias, void *out, int8_t *xq,
+                          float *xs, int64_t M, int64_t N, int64_t K, int32_t activation) {
+    if (N <= 0 || N % 16 != 0) {
+        set_error("N must be a positive multiple of 16");
+        return 2;
+    }
+    if (int rc = convrot_quantize(as_stream(stream), x, xq, xs, M, K, activation)) return rc;
+    return int_mm_common(as_stream(stream), kEpiDequantBf16, xq, w8, out, xs, w_scale, bias, M, N,
+                         K, 0, N);
+}
+
+int64_t xpuint8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t inner, int32_t activation) {
+    if (M <= 0 || K <= 0 || inner <= 0) return -1;
+    return static_cast<int64_t>(ffn_layout(M, K, inner, activation).total);
+}
+
+int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
+                       const float *up_scale, const int8_t *down_w8, const float *down_scale,
+                       const float *down_bias, void *out, void *workspace, int64_t M, int64_t K,
+                       int64_t inner, int32_t activation) {
+    cudaStream_t s = as_stream(stream);
+    if (activation != 3 && activation != 4 && activation != 5) {
+        set_error("the fused FFN supports activation 3 (situ), 4 (GEGLU) or 5 (GELU-erf)");
+        return 6;
+    }
+    if (int rc = check_mk(M, K)) return rc;
+    if (inner <= 0 || inner % 256 != 0) {
+        set_error("the FFN's inner width must be a positive multiple of 256");
+        return 3;
+    }
+    if (!workspace || !aligned16(workspace)) {
+        set_error("the FFN workspace must be a 16-byte aligned buffer");
+        return 2;
+    }
+    const FfnLayout L = ffn_layout(M, K, inner, activation);
+    char *ws = static_cast<char *>(workspace);
+    int8_t *xq = reinterpret_cast<int8_t *>(ws + L.xq);
+    float *xs = reinterpret_cast<float *>(ws + L.xs);
+    int8_t *q2 = reinterpret_cast<int8_t *>(ws + L.q2);
+    float *xs2 = reinterpret_cast<float *>(ws + L.xs2);
+    if (int rc = convrot_quantize(s, x, xq, xs, M, K, 0)) return rc;
+    if (activation == 4) {
+        void *y = ws + L.mid;
+        if (int rc = int_mm_common(s, kEpiGegluBf16, xq, up_w8, y, xs, up_scale, nullptr, M, inner,
+                                   K, 0, inner))
+            return rc;
+        if (int rc = convrot_quantize(s, y, q2, xs2, M, inner, 0)) return rc;
+    } else {
+        int32_t *acc = reinterpret_cast<int32_t *>(ws + L.mid);
+        const int64_t n_up = activation == 5 ? inner : 2 * inner;
+        if (int rc = int_mm_common(s, kEpiRawI32, xq, up_w8, acc, nullptr, nullptr, nullptr, M,
+                                   n_up, K, 0, n_up))
+            return rc;
+        if (int rc = dequant_act_quantize(s, acc, q2, xs2, xs, up_scale, M, inner, activation))
+            return rc;
+    }
+    return int_mm_common(s, kEpiDequantBf16, q2, down_w8, out, xs2, down_scale, down_bias, M, K,
+                         inner, 0, K);
+}
+
+int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *col_scale,
+                                int8_t *q, float *scale, int64_t M, int64_t K) {
+    if (M <= 0 || K <= 0) {
+        set_error("M and K must be positive");
+        return 2;
+    }
+    if (!x || !q || !scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    return launch_quantize_row(as_stream(stream), x, col_scale, q, scale, M, K);
+}
+
+int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_scale, int8_t *gq,
+                            float *tg, int64_t M, int64_t N) {
+    if (M <= 0 || N <= 0 || N % 16 != 0) {
+        set_error("M, N must be positive and N must be a multiple of 16");
+        return 2;
+    }
+    if (int rc = check_ptrs({dy, gq, tg})) return rc;
+    if (!x_scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    return launch_colquant(as_stream(stream), dy, x_scale, gq, tg, M, N);
+}
+
+int xpuint8_fault_status(int32_t reset) { return gemm_fault_status(reset); }
+
+}  // extern "C"

@@ -1,0 +1,221 @@
+// Shared device helpers for libxpuint8 (sm_100a): bf16 conversions, the
+// radix-4 ConvRot butterflies, and thin inline-PTX wrappers for mbarrier,
+// TMA (cp.async.bulk.tensor) and the tcgen05 tensor-core / TMEM instructions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xpuint8 {
+
+constexpr int kGroup = 256;  // ConvRot group size (a power of 4; 4 radix-4 digits)
+
+// ---------------------------------------------------------------------------
+// bf16 <-> fp32 (bit-level: exact widening, round-to-nearest-even narrowing)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+// round-to-nearest-even fp32 -> bf16 bits; NaN -> canonical quiet NaN
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0u;
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return u >> 16;
+}
+__device__ __forceinline__ float round_bf16(float f) {
+    return __uint_as_float(f32_to_bf16_bits(f) << 16);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
+}
+
+// 16 packed bf16 (two 16-byte words) -> 16 fp32
+__device__ __forceinline__ void unpack16_bf16(const uint4 &a, const uint4 &b, float (&v)[16]) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        v[2 * j] = bf16_lo(w[j]);
+        v[2 * j + 1] = bf16_hi(w[j]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The radix-4 ConvRot butterflies, without the 1/2 factor of each stage.
+//
+// H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]]; one stage is H4/2.  The
+// 1/2 of the four stages is applied once at the end (x 1/16): a power-of-two
+// scaling commutes with fp32 rounding, so the result carries exactly the bits
+// of the per-stage form for every normal-range value.
+//
+// axis_seq: the accumulation-chain association, out_r = ((h0 a0 + h1 a1) + h2
+//   a2) + h3 a3.  The shared first partial sums give 2.5 adds per element.
+// axis_bfly: the butterfly association, p=a0+a1, m=a0-a1, q=a2+a3, n=a2-a3,
+//   out = (p+n, p-n, m+q, q-m).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void axis_seq(float &a0, float &a1, float &a2, float &a3) {
+    const float p = __fadd_rn(a0, a1), m = __fsub_rn(a0, a1);
+    const float o0 = __fsub_rn(__fadd_rn(p, a2), a3);
+    const float o1 = __fadd_rn(__fsub_rn(p, a2), a3);
+    const float o2 = __fadd_rn(__fadd_rn(m, a2), a3);
+    const float o3 = __fadd_rn(__fsub_rn(a2, m), a3);
+    a0 = o0; a1 = o1; a2 = o2; a3 = o3;
+}
+__device__ __forceinline__ void axis_bfly(float &a0, float &a1, float &a2, float &a3) {
+    const float p = __fadd_rn(a0, a1), m = __fsub_rn(a0, a1);
+    const float q = __fadd_rn(a2, a3), n = __fsub_rn(a2, a3);
+    a0 = __fadd_rn(p, n); a1 = __fsub_rn(p, n); a2 = __fadd_rn(m, q); a3 = __fsub_rn(q, m);
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// A wait that always ends.  It gives up after kWaitTimeoutNs of wall time (or
+// kWaitMaxIters polls), records `site` in *fault (first writer wins) and
+// returns false; it also returns false as soon as another thread has recorded
+// a fault, so every role of every CTA leaves its loop within a bounded time.
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr uint32_t kWaitMaxIters = 1u << 28;
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *fault, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1; it < kWaitMaxIters; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0u) {
+            if (*reinterpret_cast<volatile int *>(fault) != 0) return false;
+            if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+        }
+    }
+    atomicCAS(fault, 0, site);
+    return false;
+}
+
+// TMA: 2-D tiled bulk tensor load into this CTA's shared memory, completing
+// `bytes` on the mbarrier.  x is the innermost coordinate (elements).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int x,
+                                            int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// tcgen05: TMEM allocation (one full warp), MMA issue and commit (one thread),
+// TMEM -> register loads (one warp per 32-lane quarter).
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// 32 TMEM lanes x 32-bit, 32 consecutive columns: thread t of the warp gets
+// lane (base_lane + t), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+
+// UMMA shared-memory matrix descriptor, 128-byte swizzle (sm100 version 1).
+//   bits  0-13  start address >> 4
+//   bits 16-29  leading-dimension byte offset >> 4
+//   bits 32-45  stride-dimension byte offset >> 4
+//   bits 46-47  version (1)
+//   bits 61-63  layout (2 = SWIZZLE_128B)
+__device__ __forceinline__ uint64_t umma_sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+// UMMA instruction descriptor for kind::i8 (signed x signed -> s32).
+//   bits 4-5 D format (2 = S32), 7-9 A format (1 = S8), 10-12 B format (1 = S8),
+//   bit 15/16 A/B major (0 = K, 1 = MN), 17-22 N>>3, 24-28 M>>4
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N, bool a_mn, bool b_mn) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+}  // namespace xpuint8

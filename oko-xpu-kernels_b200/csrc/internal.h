@@ -1,0 +1,53 @@
+// Host-side declarations shared between the translation units of libxpuint8.
+// Every launcher validates nothing the C entry points already validated; it
+// enqueues on `stream` and returns 0, or 5 with the error recorded.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace xpuint8 {
+
+// error reporting (abi.cu): thread-local message read by xpuint8_last_error
+void set_error(const std::string &msg);
+int launch_status(const char *what);  // cudaGetLastError -> 0 or 5 (+ message)
+int num_sms();                        // SM count of the current device
+
+// rotation family (rotate.cu)
+//   mode: 0 = activation bf16 -> int8 (act 0..5), 1 = dequant+act int32 -> int8 (act 3,4,5),
+//         2 = rotate bf16 -> bf16, 3 = dequant_weight int8 -> bf16
+int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const float *w_scale,
+                       const float *x_scale, void *out, float *scale, int64_t M, int64_t K);
+
+// dequant epilogue (epilogue.cu)
+int launch_dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float *x_scale,
+                            const float *w_scale, const float *bias, int64_t M, int64_t N,
+                            int64_t acc_row_stride);
+
+// row / column quantizers (rowquant.cu)
+int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, int8_t *q,
+                        float *scale, int64_t M, int64_t K);
+int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t *gq, float *tg,
+                    int64_t M, int64_t N);
+
+// tcgen05 int8 GEMM (gemm_i8.cu)
+enum GemmEpilogue { kEpiRawI32 = 0, kEpiDequantBf16 = 1, kEpiGegluBf16 = 2 };
+struct GemmCall {
+    int epilogue = kEpiRawI32;
+    const int8_t *a = nullptr;  // [M,K] (a_mn=0) or [K,M] (a_mn=1), row stride lda
+    const int8_t *b = nullptr;  // [N,K] (b_mn=0) or [K,N] (b_mn=1), row stride ldb
+    bool a_mn = false, b_mn = false;
+    int64_t lda = 0, ldb = 0;
+    void *out = nullptr;        // int32 or bf16 [M, N], row stride ldo (elements)
+    int64_t ldo = 0;
+    const float *row_scale = nullptr;  // [M]  (x_scale)
+    const float *col_scale = nullptr;  // [N]  (w_scale) or null = 1; GEGLU: [2N]
+    const float *bias = nullptr;       // [N]  or null
+    int64_t M = 0, N = 0, K = 0;       // GEGLU: N = output width (half of B's rows)
+};
+int launch_gemm(cudaStream_t s, const GemmCall &c);
+int gemm_fault_status(int reset);  // device fault word of the GEMM waits
+
+}  // namespace xpuint8

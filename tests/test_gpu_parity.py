@@ -1,0 +1,423 @@
+"""GPU parity: every CUDA kernel against the CPU oracle on the same seeded inputs.
+
+Integer and byte results must be bit-exact (int32 accumulators, int8 codes of
+the pure rotation paths, bf16 outputs of the rotation / dequant paths whose
+fp32 arithmetic the oracle restates operation for operation).  Where a device
+transcendental (erf, tanh, exp) enters, codes may differ by 1 at a rate below
+1e-3 and bf16 outputs by a relative L2 of 1e-2, the north-star tolerance.
+
+Large shapes are checked through size-independent properties: rows are
+independent in every kernel of the forward, so a sample of rows of a full-size
+call is compared exactly with the oracle run on those rows alone.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import convrot_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    import xpu_kernels
+    from xpu_kernels.int8 import _lib as L
+    if not torch.cuda.is_available():
+        pytest.fail("no CUDA device")
+    if not xpu_kernels.available():
+        pytest.fail(f"libxpuint8 did not load: {L._ERR}")
+    yield
+    torch.cuda.synchronize()
+    assert L.load().xpuint8_fault_status(1) == 0
+
+
+def bits(t):
+    """torch tensor -> numpy (bf16 as uint16 bits)."""
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def dev_bf16(a):
+    """numpy uint16 bits -> CUDA bf16 tensor."""
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(DEV)
+
+
+def rand_bf16(shape, seed, scale=1.0, outliers=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=g) * scale
+    if outliers:
+        cols = torch.randperm(shape[-1], generator=g)[:outliers]
+        x[..., cols] *= 20
+    return x.to(torch.bfloat16)
+
+
+def rand_i8(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(-127, 128, shape, generator=g, dtype=torch.int8)
+
+
+def codes_close(got, ref, rate=1e-4):
+    d = np.abs(got.astype(np.int16) - ref.astype(np.int16))
+    assert d.max() <= 1, f"max code difference {d.max()}"
+    assert (d > 0).mean() < rate, f"mismatch rate {(d > 0).mean():.2e}"
+
+
+def scales_close(got, ref, ulps=1):
+    gi = got.view(np.int32).astype(np.int64)
+    ri = ref.view(np.int32).astype(np.int64)
+    assert np.abs(gi - ri).max() <= ulps
+
+
+def rel_l2(a, b):
+    a = O.bf16_bits_to_f32(a).astype(np.float64) if a.dtype == np.uint16 else a.astype(np.float64)
+    b = O.bf16_bits_to_f32(b).astype(np.float64) if b.dtype == np.uint16 else b.astype(np.float64)
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+SHAPES = [(1, 256), (3, 1024), (127, 1280), (300, 4096), (37, 5120), (9, 10240), (5, 32768)]
+
+
+# ------------------------------------------------------------------------ rotation family
+
+@pytest.mark.parametrize("m,k", SHAPES)
+def test_rotate_bf16_is_bit_exact(m, k):
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 10 + k, outliers=4)
+    got = bits(int8.rotate(x.to(DEV)))
+    assert np.array_equal(got, O.rotate_bf16(bits(x)))
+
+
+@pytest.mark.parametrize("m,k", SHAPES)
+def test_quantize_is_bit_exact(m, k):
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 20 + k, outliers=8)
+    q, s = int8.quantize(x.to(DEV))
+    qr, sr = O.convrot_quantize(bits(x))
+    assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
+    assert np.array_equal(bits(q), qr)
+
+
+def test_quantize_edge_rows():
+    from xpu_kernels import int8
+    x = torch.zeros(6, 512, dtype=torch.bfloat16)
+    x[1, 7] = 1.0                       # one-hot row
+    x[2] = -3.0                         # constant row
+    x[3, ::2] = 1e-20                   # tiny values
+    x[4] = rand_bf16((512,), 5) * 1e4   # large values
+    x[5, :4] = torch.tensor([127.0, 254.0, -254.0, 63.0])
+    q, s = int8.quantize(x.to(DEV))
+    qr, sr = O.convrot_quantize(bits(x))
+    assert np.array_equal(bits(q), qr)
+    assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
+    assert bits(s)[0] == np.float32(1e-30) and not bits(q)[0].any()
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "swiglu", "situ", "geglu_erf", "gelu_erf"])
+@pytest.mark.parametrize("m,k", [(5, 256), (64, 1280), (33, 4096)])
+def test_quantize_act(act, m, k):
+    from xpu_kernels import int8
+    kin = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
+    x = rand_bf16((m, kin), 30 + k, scale=2.0)
+    q, s = int8.quantize_act(x.to(DEV), act)
+    qr, sr = O.convrot_quantize(bits(x), int8.ACTIVATIONS[act])
+    codes_close(bits(q), qr, rate=1e-3)
+    scales_close(bits(s), sr, ulps=2 ** 16)  # a 1-ulp bf16 activation can move the row max
+    assert np.abs(bits(s) / sr - 1).max() < 1e-2
+
+
+@pytest.mark.parametrize("n,k", [(16, 256), (300, 1280), (64, 5120)])
+def test_dequant_weight_is_bit_exact(n, k):
+    from xpu_kernels import int8
+    w8 = rand_i8((n, k), 40 + k)
+    g = torch.Generator().manual_seed(41)
+    ws = torch.rand(n, generator=g) * 0.01 + 1e-4
+    got = bits(int8.dequant_weight(w8.to(DEV), ws.to(DEV)))
+    assert np.array_equal(got, O.dequant_weight(bits(w8), bits(ws)))
+    # and it is the torch chain of the reference
+    chain = bits(int8.dequant_weight_torch(w8.to(DEV), ws.to(DEV)))
+    assert np.array_equal(got, chain)
+
+
+@pytest.mark.parametrize("act", ["situ", "geglu_erf", "gelu_erf"])
+@pytest.mark.parametrize("m,k", [(7, 256), (64, 1280), (19, 5120)])
+def test_dequant_act_quantize(act, m, k):
+    from xpu_kernels import int8
+    n = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
+    g = torch.Generator().manual_seed(50 + k)
+    acc = torch.randint(-200000, 200000, (m, n), generator=g, dtype=torch.int32)
+    xs = torch.rand(m, generator=g) * 1e-3 + 1e-5
+    ws = torch.rand(n, generator=g) * 1e-3 + 1e-5
+    q, s = int8.dequant_act_quantize(acc.to(DEV), xs.to(DEV), ws.to(DEV), act)
+    qr, sr = O.dequant_act_quantize(bits(acc), bits(xs), bits(ws), int8.ACTIVATIONS[act])
+    codes_close(bits(q), qr, rate=1e-3)
+    assert np.abs(bits(s) / sr - 1).max() < 1e-2
+
+
+# ------------------------------------------------------------------------ dequant epilogue
+
+@pytest.mark.parametrize("m,n", [(1, 16), (129, 272), (300, 1280)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_dequant_epilogue_is_bit_exact(m, n, with_bias):
+    from xpu_kernels import int8
+    g = torch.Generator().manual_seed(60 + n)
+    acc = torch.randint(-(2 ** 24), 2 ** 24, (m, n), generator=g, dtype=torch.int32)
+    xs = torch.rand(m, generator=g) * 1e-3
+    ws = torch.rand(n, generator=g) * 1e-2
+    b = torch.randn(n, generator=g) * 0.1 if with_bias else None
+    got = bits(int8.dequant(acc.to(DEV), xs.to(DEV), ws.to(DEV), None if b is None else b.to(DEV)))
+    ref = O.dequant_epilogue(bits(acc), bits(xs), bits(ws), None if b is None else bits(b))
+    assert np.array_equal(got, ref)
+
+
+def test_dequant_slice_reads_in_place():
+    from xpu_kernels import int8
+    g = torch.Generator().manual_seed(70)
+    big = torch.randint(-(2 ** 20), 2 ** 20, (77, 3 * 320), generator=g, dtype=torch.int32).to(DEV)
+    xs = (torch.rand(77, generator=g) * 1e-3).to(DEV)
+    ws = (torch.rand(320, generator=g) * 1e-2).to(DEV)
+    for j in range(3):
+        sl = big[:, j * 320:(j + 1) * 320]
+        got = int8.dequant_slice(sl, xs, ws)
+        ref = int8.dequant(sl.contiguous(), xs, ws)
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    # an odd offset (not 16-byte aligned) takes the scalar path
+    sl = big[:, 3:3 + 320]
+    assert torch.equal(int8.dequant_slice(sl, xs, ws).view(torch.int16),
+                       int8.dequant(sl.contiguous(), xs, ws).view(torch.int16))
+
+
+# ------------------------------------------------------------------------ the int8 GEMM
+
+GEMM_SHAPES = [(1, 16, 256), (129, 272, 1280), (300, 1024, 4096), (128, 256, 128),
+               (257, 528, 48), (2048, 1280, 1280)]
+
+
+def _exact(a, b):
+    return (a.astype(np.float64) @ b.astype(np.float64)).astype(np.int32)
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_int_mm_nt_is_bit_exact(m, n, k):
+    from xpu_kernels import int8
+    a, b = rand_i8((m, k), 80 + m), rand_i8((n, k), 81 + n)
+    got = bits(int8.int_mm(a.to(DEV), b.to(DEV), 0))
+    assert np.array_equal(got, _exact(bits(a), bits(b).T))
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_int_mm_nn_is_bit_exact(m, n, k):
+    from xpu_kernels import int8
+    a, b = rand_i8((m, k), 90 + m), rand_i8((k, n), 91 + n)
+    got = bits(int8.int_mm(a.to(DEV), b.to(DEV), 1))
+    assert np.array_equal(got, _exact(bits(a), bits(b)))
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+def test_int_mm_tn_is_bit_exact(m, n, k):
+    from xpu_kernels import int8
+    if m % 16:
+        pytest.skip("an MN-major A needs M % 16 == 0 (its row length)")
+    a, b = rand_i8((k, m), 100 + m), rand_i8((k, n), 101 + n)
+    got = bits(int8.int_mm(a.to(DEV), b.to(DEV), 2))
+    assert np.array_equal(got, _exact(bits(a).T, bits(b)))
+
+
+def test_int_mm_extreme_values_do_not_overflow():
+    from xpu_kernels import int8
+    k = 4096
+    a = torch.full((128, k), -127, dtype=torch.int8)
+    b = torch.full((256, k), -127, dtype=torch.int8)
+    got = int8.int_mm(a.to(DEV), b.to(DEV))
+    assert int(got.min()) == int(got.max()) == 127 * 127 * k
+
+
+@pytest.mark.parametrize("m,n,k", [(129, 272, 1280), (2048, 1280, 1280)])
+def test_gemm_dequant_epilogue_is_bit_exact(m, n, k):
+    from xpu_kernels import int8
+    from xpu_kernels.int8 import _lib as L
+    lib = L.load()
+    a, b = rand_i8((m, k), 110), rand_i8((n, k), 111)
+    g = torch.Generator().manual_seed(112)
+    xs, ws, bias = torch.rand(m, generator=g) * 1e-3, torch.rand(n, generator=g) * 1e-2, \
+        torch.randn(n, generator=g) * 0.1
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    ad, bd, xsd, wsd, bdd = (t.to(DEV) for t in (a, b, xs, ws, bias))
+    rc = lib.xpuint8_int_mm_dequant_stream(L._stream(out.device), L._ptr(ad), L._ptr(bd),
+                                           L._ptr(out), L._ptr(xsd), L._ptr(wsd), L._ptr(bdd),
+                                           m, n, k, 0, n)
+    assert rc == 0, lib.xpuint8_last_error()
+    ref = O.dequant_epilogue(_exact(bits(a), bits(b).T), bits(xs), bits(ws), bits(bias))
+    assert np.array_equal(bits(out), ref)
+    # and equal to the standalone epilogue on the raw accumulator
+    acc = int8.int_mm(ad, bd)
+    assert torch.equal(int8.dequant(acc, xsd, wsd, bdd).view(torch.int16), out.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,inner,k", [(64, 256, 256), (300, 1280, 1280)])
+def test_gemm_geglu_epilogue(m, inner, k):
+    from xpu_kernels.int8 import _lib as L
+    lib = L.load()
+    a, b = rand_i8((m, k), 120), rand_i8((2 * inner, k), 121)
+    g = torch.Generator().manual_seed(122)
+    xs, ws = torch.rand(m, generator=g) * 1e-3, torch.rand(2 * inner, generator=g) * 1e-2
+    y = torch.empty((m, inner), dtype=torch.bfloat16, device=DEV)
+    ad, bd, xsd, wsd = (t.to(DEV) for t in (a, b, xs, ws))
+    rc = lib.xpuint8_int_mm_geglu_stream(L._stream(y.device), L._ptr(ad), L._ptr(bd), L._ptr(y),
+                                         L._ptr(xsd), L._ptr(wsd), m, inner, k)
+    assert rc == 0, lib.xpuint8_last_error()
+    acc = _exact(bits(a), bits(b).T)
+    d = O.round_bf16((acc.astype(np.float32) * (bits(ws)[None, :] * bits(xs)[:, None]).astype(np.float32)).astype(np.float32))
+    ref = O.f32_to_bf16_bits(O.activation(4, d[:, :inner], d[:, inner:]))
+    got = bits(y)
+    assert (got != ref).mean() < 1e-3        # erf differs from the oracle's in rare last bits
+    assert rel_l2(got, ref) < 1e-3
+
+
+# ------------------------------------------------------------------------ compositions
+
+def _prep(n, k, seed):
+    w = rand_bf16((n, k), seed, scale=0.02)
+    w8, ws = O.prepare_weight(bits(w))
+    return w, w8, ws
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 1024, 1024), (77, 272, 512)])
+def test_linear_matches_the_oracle(m, n, k):
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 130, outliers=8)
+    _, w8, ws = _prep(n, k, 131)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(132)) * 0.01)
+    got = bits(int8.linear(x.to(DEV), torch.from_numpy(w8).to(DEV), torch.from_numpy(ws).to(DEV),
+                           bias.to(DEV)))
+    ref = O.linear(bits(x), w8, ws, bits(bias))
+    assert np.array_equal(got, ref)
+
+
+def test_prepare_weight_matches_the_reference_fixture():
+    from xpu_kernels import int8
+    import os
+    G = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_cpu.npz"))
+    q, s = int8.prepare_weight(dev_bf16(G["pw_w"]))
+    assert np.array_equal(bits(q), G["pw_q"])
+    assert np.array_equal(bits(s).view(np.uint32), G["pw_s"].view(np.uint32))
+    dq = int8.dequant_weight(q, s)
+    assert np.array_equal(bits(dq), G["dq_w"])
+    dx = int8.linear_dx_int8(dev_bf16(G["dx_dy"]), q, s)
+    assert np.array_equal(bits(dx), G["dx_out"])
+
+
+def test_quantize_row_matches_the_reference_fixture():
+    from xpu_kernels import int8
+    import os
+    G = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_cpu.npz"))
+    q, s = int8.quantize_row(dev_bf16(G["qrow_x"]))
+    assert np.array_equal(bits(q), G["qrow_q"])
+    assert np.array_equal(bits(s).view(np.uint32), G["qrow_s"].view(np.uint32))
+    tie = torch.tensor([[127.0, 254.0, -254.0, 63.0] + [0.0] * 4], dtype=torch.bfloat16)
+    q, _ = int8.quantize_row(tie.to(DEV))
+    assert bits(q)[0, :4].tolist() == [64, 127, -127, 32]
+
+
+@pytest.mark.parametrize("m,k", [(64, 5120), (3, 24), (100, 1000)])
+def test_quantize_row_is_bit_exact(m, k):
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 140 + k, scale=1e-3)
+    q, s = int8.quantize_row(x.to(DEV))
+    qr, sr = O.quantize_row(bits(x))
+    assert np.array_equal(bits(q), qr)
+    assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
+    qt, st = int8.quantize_row_torch(x.to(DEV))
+    assert torch.equal(qt.cpu(), torch.from_numpy(qr))
+
+
+def test_linear_dx_int8_matches_the_oracle():
+    from xpu_kernels import int8
+    m, n, k = 256, 512, 1280
+    _, w8, ws = _prep(n, k, 150)
+    dy = rand_bf16((m, n), 151, scale=1e-3)
+    got = bits(int8.linear_dx_int8(dy.to(DEV), torch.from_numpy(w8).to(DEV),
+                                   torch.from_numpy(ws).to(DEV)))
+    assert np.array_equal(got, O.linear_dx_int8(bits(dy), w8, ws))
+
+
+def test_linear_dw_int8_matches_the_oracle():
+    from xpu_kernels import int8
+    m, n, k = 512, 256, 1280
+    x = rand_bf16((m, k), 160)
+    dy = rand_bf16((m, n), 161, scale=1e-3)
+    xq, xs = int8.quantize(x.to(DEV))
+    got = bits(int8.linear_dw_int8(dy.to(DEV), xq, xs))
+    ref = O.linear_dw_int8(bits(dy), bits(xq), bits(xs))
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("act", ["geglu_erf", "situ", "gelu_erf"])
+def test_ffn_matches_the_oracle(act):
+    from xpu_kernels import int8
+    m, k, inner = 96, 512, 768
+    n_up = 2 * inner if act in int8.PAIRED_ACTIVATIONS else inner
+    x = rand_bf16((m, k), 170)
+    _, up8, up_s = _prep(n_up, k, 171)
+    _, dn8, dn_s = _prep(k, inner, 172)
+    got = bits(int8.ffn(x.to(DEV), torch.from_numpy(up8).to(DEV), torch.from_numpy(up_s).to(DEV),
+                        torch.from_numpy(dn8).to(DEV), torch.from_numpy(dn_s).to(DEV), act=act))
+    ref = O.ffn(bits(x), up8, up_s, dn8, dn_s, None, int8.ACTIVATIONS[act])
+    assert rel_l2(got, ref) < 1e-2
+    assert (got != ref).mean() < 0.05
+
+
+def test_geglu_ffn_equals_the_unfused_chain():
+    # the reference's self-test: fused GEGLU FFN == dequant -> hidden*gelu(gate) -> quantize
+    from xpu_kernels import int8
+    m, k, inner = 128, 1280, 1280
+    x = rand_bf16((m, k), 180).to(DEV)
+    w1 = rand_bf16((2 * inner, k), 181, scale=0.02).to(DEV)
+    w2 = rand_bf16((k, inner), 182, scale=0.02).to(DEV)
+    up8, up_s = int8.prepare_weight(w1)
+    dn8, dn_s = int8.prepare_weight(w2)
+    fused = int8.ffn(x, up8, up_s, dn8, dn_s, act="geglu_erf")
+    acc, xs = int8.linear_acc(x, up8, up_s)
+    d = int8.dequant(acc, xs, up_s)
+    h, gt = d.chunk(2, dim=-1)
+    q2, xs2 = int8.quantize(h * torch.nn.functional.gelu(gt))
+    chain = int8.dequant(int8.int_mm(q2, dn8), xs2, dn_s)
+    assert (fused.view(torch.int16) != chain.view(torch.int16)).float().mean().item() < 1e-3
+
+
+def test_selftest_passes():
+    from xpu_kernels import int8
+    assert int8.selftest(verbose=True)
+
+
+# ------------------------------------------------------------------------ full-size properties
+
+@pytest.mark.parametrize("cfg", ["C2", "C3", "C4", "C5"])
+def test_full_size_linear_on_sampled_rows(cfg):
+    """The BASELINE configs at full size: every row of the output is independent,
+    so sampled rows are checked bit for bit against the oracle."""
+    from xpu_kernels import int8
+    m, k, n, seed = {"C2": (2048, 1280, 1280, 1), "C3": (2048, 1280, 10240, 2),
+                     "C4": (4096, 1280, 5120, 3), "C5": (65536, 4096, 14336, 4)}[cfg]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g)
+    x[:, torch.randperm(k, generator=g)[:max(1, k // 100)]] *= 10
+    x = x.to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    w8, ws = int8.prepare_weight(w)
+    y = int8.linear(x, w8, ws)
+    rows = torch.randperm(m, generator=g)[:24].sort().values
+    ref = O.linear(bits(x[rows.to(DEV)]), bits(w8), bits(ws))
+    assert np.array_equal(bits(y[rows.to(DEV)]), ref)
+    # and the accumulators of those rows are exact
+    acc, xs = int8.linear_acc(x, w8, ws)
+    xq_rows, _ = O.convrot_quantize(bits(x[rows.to(DEV)]))
+    assert np.array_equal(bits(acc[rows.to(DEV)]), _exact(xq_rows, bits(w8).T))
+    rel = torch.linalg.norm((y.float() - (x.float() @ w.float().t()))) / \
+        torch.linalg.norm(x.float() @ w.float().t())
+    assert rel.item() < 2e-2
