@@ -494,6 +494,11 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
     return launch_colquant(as_stream(stream), dy, x_scale, gq, tg, M, N);
 }
 
-int xpuint8_fault_status(int32_t reset) { return gemm_fault_status(reset); }
+int xpuint8_fault_status(int32_t reset) {
+    const int g = gemm_fault_status(reset);
+    const int r = rot_fault_status(reset);
+    if (g < 0 || r < 0) return -1;
+    return g != 0 ? g : r;
+}
 
 }  // extern "C"

@@ -52,7 +52,8 @@ constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BY
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 2 * BN;
 constexpr int GROUP_M = 16;
-constexpr size_t kSmemBytes = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + 256;
+constexpr size_t kSmemBytes =
+    static_cast<size_t>(STAGES) * STAGE_BYTES + 4 * 2 * 32 * 64 + 2 * BN * 4 + 1024 + 256;
 
 struct GemmArgs {
     void *out;
@@ -85,86 +86,137 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     atomicCAS(&g_gemm_fault, 0, 99);
 }
 
+// Epilogue staging.  Each epilogue warp owns two 2 KB buffers of 32 rows x 64
+// bytes (64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r>>1)&3),
+// the pattern the TMA store unswizzles).  A 32-column chunk of the warp's 32
+// rows (bf16; int32 uses 16-column chunks) is converted in registers, written
+// to one buffer and handed to a TMA bulk-tensor store, which also clips the
+// M/N tails; the other buffer is filled meanwhile.
+constexpr int kStageBytes = 32 * 64;
+constexpr int kEpiSmem = 4 * 2 * kStageBytes;  // 4 warps x 2 buffers
+
+__device__ __forceinline__ uint32_t stage_chunk_addr(uint32_t buf, int row, int c) {
+    return buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4);
+}
+
+// one 32-column chunk of bf16 output: v[0..31] are the fp32 results of this row
+__device__ __forceinline__ void stage_bf16_32(uint32_t buf, int lane, const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        st_shared_v4(stage_chunk_addr(buf, lane, c), cvt_bf16x2(v[8 * c], v[8 * c + 1]),
+                     cvt_bf16x2(v[8 * c + 2], v[8 * c + 3]), cvt_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                     cvt_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+}
+
+// hand a filled buffer to the TMA unit (one lane), then flip buffers
+__device__ __forceinline__ void stage_flush(const void *tmap, uint32_t buf, int lane, int x, int y) {
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmap, buf, x, y);
+        bulk_commit();
+    }
+}
+// before refilling a buffer: its previous store must have read it
+__device__ __forceinline__ void stage_reserve(int lane) {
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+}
+
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs &a, uint32_t taddr, int row,
-                                               int col0, float xs, bool row_ok) {
-    uint32_t r[32];
-    tmem_ld32(taddr, r);
-    if constexpr (EPI == kEpiGegluBf16) {
-        uint32_t gt[32];
-        tmem_ld32(taddr + 128, gt);
-        tmem_wait_ld();
-        if (!row_ok || col0 >= a.N) return;
-        uint32_t packed[16];
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmOut, uint32_t taddr,
+                                              int m0, int n0, int quarter, int lane, float xs,
+                                              const float *s_ws, const float *s_b, uint32_t bufs,
+                                              int &bsel) {
+    const int y = m0 + quarter * 32;
+    if constexpr (EPI == kEpiRawI32) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            if (n0 + c * 32 >= a.N) break;
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            const float4 wh = __ldg(reinterpret_cast<const float4 *>(a.col_scale + col0 + j));
-            const float4 wg = __ldg(reinterpret_cast<const float4 *>(a.col_scale + a.N + col0 + j));
-            const float whv[4] = {wh.x, wh.y, wh.z, wh.w};
-            const float wgv[4] = {wg.x, wg.y, wg.z, wg.w};
-            float y[4];
+            for (int h = 0; h < 2; ++h) {
+                stage_reserve(lane);
+                const uint32_t buf = bufs + bsel * kStageBytes;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float h = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j + t])),
-                                                     __fmul_rn(whv[t], xs)));
-                const float g = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(gt[j + t])),
-                                                     __fmul_rn(wgv[t], xs)));
-                const float ge = __fmul_rn(__fmul_rn(0.5f, g),
-                                           __fadd_rn(1.0f, erff(__fmul_rn(g, 0.7071067811865476f))));
-                y[t] = __fmul_rn(h, round_bf16(ge));
+                for (int q = 0; q < 4; ++q)
+                    st_shared_v4(stage_chunk_addr(buf, lane, q), r[16 * h + 4 * q], r[16 * h + 4 * q + 1],
+                                 r[16 * h + 4 * q + 2], r[16 * h + 4 * q + 3]);
+                stage_flush(tmOut, buf, lane, n0 + c * 32 + 16 * h, y);
+                bsel ^= 1;
             }
-            packed[j / 2] = pack_bf16x2(y[0], y[1]);
-            packed[j / 2 + 1] = pack_bf16x2(y[2], y[3]);
         }
-        uint16_t *dst = static_cast<uint16_t *>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-        d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-        if (col0 + 16 < a.N) {
-            d4[2] = make_uint4(packed[8], packed[9], packed[10], packed[11]);
-            d4[3] = make_uint4(packed[12], packed[13], packed[14], packed[15]);
-        }
-    } else {
-        tmem_wait_ld();
-        if (!row_ok || col0 >= a.N) return;
-        if constexpr (EPI == kEpiRawI32) {
-            int32_t *dst = static_cast<int32_t *>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-            int4 *d4 = reinterpret_cast<int4 *>(dst);
-            const int nv = (col0 + 16 < a.N) ? 8 : 4;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < nv)
-                    d4[j] = make_int4(static_cast<int>(r[4 * j]), static_cast<int>(r[4 * j + 1]),
-                                      static_cast<int>(r[4 * j + 2]), static_cast<int>(r[4 * j + 3]));
-        } else {  // dequant -> bf16
-            uint32_t packed[16];
+    } else if constexpr (EPI == kEpiDequantBf16) {
+        const f2 xs2 = mk2(xs, xs);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            if (n0 + c * 32 >= a.N) break;
+            uint32_t r[32];
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            float v[32];
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
-                float w[4] = {1.f, 1.f, 1.f, 1.f};
-                if (a.col_scale) {
-                    const float4 wv = __ldg(reinterpret_cast<const float4 *>(a.col_scale + col0 + j));
-                    w[0] = wv.x; w[1] = wv.y; w[2] = wv.z; w[3] = wv.w;
-                }
-                float v[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    v[t] = __fmul_rn(static_cast<float>(static_cast<int32_t>(r[j + t])), __fmul_rn(w[t], xs));
+                const float4 w = *reinterpret_cast<const float4 *>(s_ws + c * 32 + j);
+                const float4 b = *reinterpret_cast<const float4 *>(s_b + c * 32 + j);
+                // float(acc) * (w_scale[n] * x_scale[m]) + bias[n], each op rounded
+                f2 s01 = mul2(mk2(w.x, w.y), xs2), s23 = mul2(mk2(w.z, w.w), xs2);
+                f2 p01 = mul2(mk2(static_cast<float>(static_cast<int32_t>(r[j])),
+                                  static_cast<float>(static_cast<int32_t>(r[j + 1]))), s01);
+                f2 p23 = mul2(mk2(static_cast<float>(static_cast<int32_t>(r[j + 2])),
+                                  static_cast<float>(static_cast<int32_t>(r[j + 3]))), s23);
                 if (a.bias) {
-                    const float4 bv = __ldg(reinterpret_cast<const float4 *>(a.bias + col0 + j));
-                    v[0] = __fadd_rn(v[0], bv.x); v[1] = __fadd_rn(v[1], bv.y);
-                    v[2] = __fadd_rn(v[2], bv.z); v[3] = __fadd_rn(v[3], bv.w);
+                    p01 = add2(p01, mk2(b.x, b.y));
+                    p23 = add2(p23, mk2(b.z, b.w));
                 }
-                packed[j / 2] = pack_bf16x2(v[0], v[1]);
-                packed[j / 2 + 1] = pack_bf16x2(v[2], v[3]);
+                un2(p01, v[j], v[j + 1]);
+                un2(p23, v[j + 2], v[j + 3]);
             }
-            uint16_t *dst = static_cast<uint16_t *>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-            d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-            if (col0 + 16 < a.N) {
-                d4[2] = make_uint4(packed[8], packed[9], packed[10], packed[11]);
-                d4[3] = make_uint4(packed[12], packed[13], packed[14], packed[15]);
+            stage_reserve(lane);
+            const uint32_t buf = bufs + bsel * kStageBytes;
+            stage_bf16_32(buf, lane, v);
+            stage_flush(tmOut, buf, lane, n0 + c * 32, y);
+            bsel ^= 1;
+        }
+    } else {  // GEGLU: hidden columns [0,128) and gate columns [128,256) of the accumulator
+        const f2 xs2 = mk2(xs, xs);
+#pragma unroll 1
+        for (int c = 0; c < 128 / 32; ++c) {
+            if (n0 + c * 32 >= a.N) break;
+            uint32_t rh[32], rg[32];
+            tmem_ld32(taddr + c * 32, rh);
+            tmem_ld32(taddr + 128 + c * 32, rg);
+            tmem_wait_ld();
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float2 wh = *reinterpret_cast<const float2 *>(s_ws + c * 32 + j);
+                const float2 wg = *reinterpret_cast<const float2 *>(s_ws + 128 + c * 32 + j);
+                float h0, h1, g0, g1;
+                un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rh[j])),
+                             static_cast<float>(static_cast<int32_t>(rh[j + 1]))),
+                         mul2(mk2(wh.x, wh.y), xs2)), h0, h1);
+                un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rg[j])),
+                             static_cast<float>(static_cast<int32_t>(rg[j + 1]))),
+                         mul2(mk2(wg.x, wg.y), xs2)), g0, g1);
+                // h, g rounded to bf16 (the unfused chain stores them), then
+                // y = bf16(h * bf16(0.5 g (1 + erf(g / sqrt 2))))
+                h0 = round_bf16(h0); h1 = round_bf16(h1);
+                g0 = round_bf16(g0); g1 = round_bf16(g1);
+                const float e0 = __fmul_rn(__fmul_rn(0.5f, g0),
+                                           __fadd_rn(1.0f, erff(__fmul_rn(g0, 0.7071067811865476f))));
+                const float e1 = __fmul_rn(__fmul_rn(0.5f, g1),
+                                           __fadd_rn(1.0f, erff(__fmul_rn(g1, 0.7071067811865476f))));
+                v[j] = __fmul_rn(h0, round_bf16(e0));
+                v[j + 1] = __fmul_rn(h1, round_bf16(e1));
             }
+            stage_reserve(lane);
+            const uint32_t buf = bufs + bsel * kStageBytes;
+            stage_bf16_32(buf, lane, v);
+            stage_flush(tmOut, buf, lane, n0 + c * 32, y);
+            bsel ^= 1;
         }
     }
 }
@@ -172,16 +224,20 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &a, uint32_t taddr
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const uint32_t sA = smem_u32(smem);
     const uint32_t sB = sA + STAGES * A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    const uint32_t sEpi = sA + STAGES * STAGE_BYTES;  // 4 warps x 2 staging buffers
+    float *s_ws = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + kEpiSmem);
+    float *s_b = s_ws + BN;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(s_b + BN);
     const uint32_t bar0 = smem_u32(bars);
     const uint32_t final_bar = bar0 + 8 * (2 * STAGES + 4);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+    const uint32_t epi_bar = bar0 + 8 * (2 * STAGES + 5);  // the 128 epilogue threads
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 6);
 #define FULL(s) (bar0 + 8u * (s))
 #define EMPTY(s) (bar0 + 8u * (STAGES + (s)))
 #define TFULL(a) (bar0 + 8u * (2 * STAGES + (a)))
@@ -200,9 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(TEMPTY(a), 128);
         }
         mbar_init(final_bar, 1);
+        mbar_init(epi_bar, 128);
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        prefetch_tmap(&tmOut);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -222,9 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ------------------------------------------------------------ TMA producer
             int stage = 0;
             uint32_t ph = 0;
-            uint32_t last_ph[STAGES];
-            bool used[STAGES];
-            for (int s = 0; s < STAGES; ++s) { used[s] = false; last_ph[s] = 0; }
+            uint32_t issued = 0;  // k-blocks issued by this CTA
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
                 int mb, nb;
@@ -244,14 +300,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         tma_load_2d(dB, &tmB, FULL(stage), kb * BK, nb * BN);
                     }
-                    used[stage] = true;
-                    last_ph[stage] = ph;
+                    ++issued;
                     if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
             }
             // our loads must have landed before the CTA can leave
-            for (int s = 0; s < STAGES; ++s)
-                if (used[s]) drain_wait(FULL(s), last_ph[s]);
+            // the last k-block issued into ring slot s was number i (i % STAGES == s)
+            for (uint32_t s = 0; s < STAGES && s < issued; ++s) {
+                const uint32_t last = s + ((issued - 1 - s) / STAGES) * STAGES;
+                drain_wait(FULL(s), (last / STAGES) & 1u);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -295,26 +353,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------------------------------------------------------- epilogue
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+        const uint32_t bufs = sEpi + (warp - 2) * 2 * kStageBytes;
+        int bsel = 0;
         int acc = 0;
         uint32_t aph = 0;
+        uint32_t epi_phase = 0;
+        // a barrier of the 128 epilogue threads whose wait is bounded like every other
+        auto epi_sync = [&](int site) {
+            mbar_arrive(epi_bar);
+            const bool ok = mbar_wait(epi_bar, epi_phase & 1u, fault, site);
+            ++epi_phase;
+            return ok;
+        };
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
+            const int n0 = nb * BN_OUT;
+            // this tile's column scales and bias into shared memory
+            if (!epi_sync(5)) break;
+            for (int i = et; i < BN; i += 128) {
+                int n;
+                if constexpr (GEGLU) n = (i < 128) ? n0 + i : args.N + n0 + (i - 128);
+                else n = n0 + i;
+                const bool in = GEGLU ? (n0 + (i & 127)) < args.N : n < args.N;
+                s_ws[i] = (in && args.col_scale) ? __ldg(args.col_scale + n) : 1.f;
+                s_b[i] = (in && args.bias) ? __ldg(args.bias + n) : 0.f;
+            }
+            if (!epi_sync(6)) break;
             if (!mbar_wait(TFULL(acc), aph, fault, 4)) break;
             tc_fence_after();
             const int row = mb * BM + quarter * 32 + lane;
-            const bool row_ok = row < args.M;
-            const float xs = (row_ok && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
+            const float xs = (row < args.M && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN_OUT / 32; ++c)
-                epilogue_chunk<EPI>(args, taddr + c * 32, row, nb * BN_OUT + c * 32, xs, row_ok);
+            epilogue_tile<EPI>(args, &tmOut, taddr, mb * BM, n0, quarter, lane, xs, s_ws, s_b,
+                               bufs, bsel);
             tc_fence_before();
             mbar_arrive(TEMPTY(acc));
             acc ^= 1;
             if (acc == 0) aph ^= 1u;
         }
+        // the stores must have left shared memory before the CTA exits
+        if (lane == 0) bulk_wait<0>();
+        __syncwarp();
     }
 #undef FULL
 #undef EMPTY
@@ -346,10 +428,12 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D int8 tensor map: `inner` contiguous elements per row, `outer` rows, row
-// stride `ld` bytes, 128-byte swizzled boxes of box_inner x box_outer
+// 2-D tensor map: `inner` contiguous elements per row, `outer` rows, row
+// stride `ld` bytes, swizzled boxes of box_inner x box_outer elements
 bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint64_t ld,
-              uint32_t box_inner, uint32_t box_outer) {
+              uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) {
         set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -359,9 +443,8 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
     const cuuint64_t strides[1] = {ld};
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t es[2] = {1, 1};
-    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
-                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const CUresult r = enc(m, dtype, 2, const_cast<void *>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (error " + std::to_string(static_cast<int>(r)) +
@@ -372,8 +455,8 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
 }
 
 template <int EPI, bool A_MN, bool B_MN>
-int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &a,
-                int grid) {
+int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
+                const GemmArgs &a, int grid) {
     auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     static int configured_mask = 0;  // one bit per device ordinal (< 32)
     int dev = 0;
@@ -384,7 +467,7 @@ int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, co
             return launch_status("gemm (shared memory attribute)");
         if (dev < 32) configured_mask |= (1 << dev);
     }
-    kern<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, a);
+    kern<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, mo, a);
     return launch_status("gemm");
 }
 
@@ -431,6 +514,17 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     } else {
         if (!make_map(&mb, c.b, c.N, c.K, c.ldb, 128, BK)) return 2;
     }
+    // output: 32-row boxes, 64-byte rows (16 int32 or 32 bf16 columns), 64-byte swizzle
+    CUtensorMap mo;
+    if (c.epilogue == kEpiRawI32) {
+        if (!make_map(&mo, c.out, c.N, c.M, c.ldo * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_INT32,
+                      CU_TENSOR_MAP_SWIZZLE_64B))
+            return 2;
+    } else {
+        if (!make_map(&mo, c.out, c.N, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                      CU_TENSOR_MAP_SWIZZLE_64B))
+            return 2;
+    }
     GemmArgs a{};
     a.out = c.out; a.ldo = c.ldo;
     a.row_scale = c.row_scale; a.col_scale = c.col_scale; a.bias = c.bias;
@@ -446,17 +540,17 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
     switch (c.epilogue) {
         case kEpiRawI32:
-            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiRawI32, false, false>(s, ma, mb, a, grid);
-            if (!c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, false, true>(s, ma, mb, a, grid);
-            if (c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, true, true>(s, ma, mb, a, grid);
+            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiRawI32, false, false>(s, ma, mb, mo, a, grid);
+            if (!c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, false, true>(s, ma, mb, mo, a, grid);
+            if (c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, true, true>(s, ma, mb, mo, a, grid);
             break;
         case kEpiDequantBf16:
-            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiDequantBf16, false, false>(s, ma, mb, a, grid);
-            if (!c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, false, true>(s, ma, mb, a, grid);
-            if (c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, true, true>(s, ma, mb, a, grid);
+            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiDequantBf16, false, false>(s, ma, mb, mo, a, grid);
+            if (!c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, false, true>(s, ma, mb, mo, a, grid);
+            if (c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, true, true>(s, ma, mb, mo, a, grid);
             break;
         case kEpiGegluBf16:
-            return launch_inst<kEpiGegluBf16, false, false>(s, ma, mb, a, grid);
+            return launch_inst<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, grid);
         default:
             break;
     }

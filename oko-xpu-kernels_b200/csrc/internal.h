@@ -21,6 +21,11 @@ int num_sms();                        // SM count of the current device
 int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const float *w_scale,
                        const float *x_scale, void *out, float *scale, int64_t M, int64_t K);
 
+// streaming rotation for modes 0, 2, 3 (rotate_bulk.cu); -1 = shape not covered
+int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
+                       void *out, float *scale, int64_t M, int64_t K);
+int rot_fault_status(int reset);  // device fault word of the streaming rotation's waits
+
 // dequant epilogue (epilogue.cu)
 int launch_dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float *x_scale,
                             const float *w_scale, const float *bias, int64_t M, int64_t N,

@@ -297,6 +297,11 @@ int dispatch_gpl(cudaStream_t s, RotParams p, int gpl, int threads, size_t smem,
 
 int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const float *w_scale,
                        const float *x_scale, void *out, float *scale, int64_t M, int64_t K) {
+    if (mode != 1) {
+        // the streaming kernel (rotate_bulk.cu) covers every shape it fits
+        const int rc = launch_rotate_bulk(s, mode, act, in, w_scale, out, scale, M, K);
+        if (rc >= 0) return rc;
+    }
     const int64_t G = K / kGroup;
     // groups per slot: the smallest of {1,2,3,4,6,8} that fits the row into 16
     // slots (one 256-thread CTA), so K <= 32768

@@ -1,0 +1,459 @@
+// The rotation family, streaming form (modes 0, 2, 3 of rotate.cu):
+//
+//   mode 0  bf16 [M,K] ([M,2K] paired) -> act -> rotate -> int8 [M,K] + scale [M]
+//           (reference: launch_convrot_quant_warp<ACT>, src/xpuint8.cpp:450-502)
+//   mode 2  bf16 [M,K] -> rotate -> bf16 [M,K]  (launch_rotate_bf16, :588-635)
+//   mode 3  int8 [N,K] * scale [N] -> bf16 -> rotate -> bf16 [N,K]
+//           (dequant_weight_torch, python/xpu_kernels/int8/ops.py:169-191)
+//
+// Persistent CTAs walk "batches" of R consecutive rows.  A batch is contiguous
+// in HBM, so one thread moves it into shared memory with a single 1-D bulk
+// copy (cp.async.bulk ... mbarrier::complete_tx), NS batches ahead of the
+// compute; the result is staged in shared memory in its final order and
+// leaves with one bulk store.  No global load or store instruction touches the
+// data itself, and the copy engine keeps NS x batch bytes in flight per CTA.
+//
+// Arithmetic: a half-warp ("slot") owns PAIRS of 256-groups and processes the
+// two groups of a pair together as packed fp32x2 values, so every butterfly
+// step is one add/sub.f32x2 for two elements.  Lane l first holds elements
+// 16l..16l+15 of both groups (digits i0, i1 in registers: axes 0 and 1 in the
+// accumulation-chain association of the reference's `inreg`), a swizzled
+// 2 KB shared-memory transpose then gives it elements 16w + l, w = 0..15
+// (digits i2, i3 in registers: axes 2 and 3 in the butterfly association of
+// `bfly_xor`).  Same association and rounding as rotate.cu, so the two kernels
+// produce the same bits; the per-stage 1/2 factors are applied once as 1/16.
+//
+// Row abs-max: per-group maxima go through shared-memory atomics into a
+// triple-buffered per-row array; quantization (reciprocal multiply, RNE by an
+// fp32 magic add) happens after one CTA barrier.
+//
+// All waits are bounded (common.cuh: mbar_wait); on a timeout the CTA records
+// the site in g_rot_fault, drains its own bulk copies and returns.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace xpuint8 {
+
+__device__ int g_rot_fault = 0;
+
+namespace {
+
+constexpr int kSlots = 16;             // half-warps per 256-thread CTA
+constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
+
+struct BulkParams {
+    const uint8_t *in;
+    const float *row_scale;  // mode 3: the weight's per-row scale
+    uint8_t *out;
+    float *scale;            // mode 0: per-row output scale
+    int64_t M, K;
+    int G, R, nbatch, ns;
+    uint32_t in_row_bytes, out_row_bytes;
+    uint32_t in_stage_bytes, out_stage_bytes;
+};
+
+__device__ __forceinline__ float gelu_erf_f(float x) {
+    const float t = __fmul_rn(x, 0.7071067811865476f);
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(t)));
+}
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float x2 = __fmul_rn(x, x);
+    const float inner = __fmul_rn(__fmul_rn(0.7978845608028654f, x),
+                                  __fadd_rn(1.0f, __fmul_rn(0.044715f, x2)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+__device__ __forceinline__ float situ_f(float h, float g) {
+    const float tg = round_bf16(tanhf(round_bf16(__fdiv_rn(g, 4.0f))));
+    const float sg = round_bf16(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+    const float th = round_bf16(tanhf(round_bf16(__fdiv_rn(h, 25.0f))));
+    const float p = round_bf16(__fmul_rn(tg, sg));
+    return round_bf16(__fmul_rn(p, th));
+}
+template <int ACT>
+__device__ __forceinline__ float activate(float a, float b) {
+    if constexpr (ACT == 0) {
+        return a;
+    } else if constexpr (ACT == 1) {
+        return round_bf16(gelu_tanh_f(a));
+    } else if constexpr (ACT == 2) {
+        const float silu = round_bf16(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
+        return round_bf16(__fmul_rn(silu, b));
+    } else if constexpr (ACT == 3) {
+        return situ_f(a, b);
+    } else if constexpr (ACT == 4) {
+        return round_bf16(__fmul_rn(a, round_bf16(gelu_erf_f(b))));
+    } else {
+        return round_bf16(gelu_erf_f(a));
+    }
+}
+__host__ __device__ constexpr bool act_paired(int act) { return act == 2 || act == 3 || act == 4; }
+
+// the 16 values lane l owns of one group, from the staged batch
+template <int MODE, int ACT>
+__device__ __forceinline__ void load16(const BulkParams &p, uint32_t stage, int rib, int g, int l,
+                                       float (&v)[16]) {
+    if constexpr (MODE == 3) {
+        const uint4 b = *reinterpret_cast<const uint4 *>(
+            __cvta_shared_to_generic(stage + rib * p.in_row_bytes + g * 256 + l * 16));
+        const float s = __ldg(p.row_scale + rib);  // rebased by the caller
+        const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                v[4 * j + t] = round_bf16(
+                    __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * t)) & 0xFF)), s));
+    } else {
+        const uint8_t *base = reinterpret_cast<const uint8_t *>(
+            __cvta_shared_to_generic(stage + rib * p.in_row_bytes + (g * 256 + l * 16) * 2));
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(base);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(base + 16);
+        unpack16_bf16(a0, a1, v);
+        if constexpr (MODE == 0 && act_paired(ACT)) {
+            const uint4 b0 = *reinterpret_cast<const uint4 *>(base + p.K * 2);
+            const uint4 b1 = *reinterpret_cast<const uint4 *>(base + p.K * 2 + 16);
+            float u[16];
+            unpack16_bf16(b0, b1, u);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], u[t]);
+        } else if constexpr (MODE == 0 && ACT != 0) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], 0.f);
+        }
+    }
+}
+
+// accumulation-chain radix-4 butterfly (unscaled) on fp32x2 lanes
+__device__ __forceinline__ void seq2(f2 &a0, f2 &a1, f2 &a2, f2 &a3) {
+    const f2 p = add2(a0, a1), m = sub2(a0, a1);
+    const f2 o0 = sub2(add2(p, a2), a3);
+    const f2 o1 = add2(sub2(p, a2), a3);
+    const f2 o2 = add2(add2(m, a2), a3);
+    const f2 o3 = add2(sub2(a2, m), a3);
+    a0 = o0; a1 = o1; a2 = o2; a3 = o3;
+}
+// butterfly-association radix-4 butterfly (unscaled) on fp32x2 lanes
+__device__ __forceinline__ void bfly2(f2 &a0, f2 &a1, f2 &a2, f2 &a3) {
+    const f2 p = add2(a0, a1), m = sub2(a0, a1);
+    const f2 q = add2(a2, a3), n = sub2(a2, a3);
+    a0 = add2(p, n); a1 = sub2(p, n); a2 = add2(m, q); a3 = sub2(q, m);
+}
+
+// Rotate a pair of groups.  In: P[q] = (A[16l+q], B[16l+q]).  Out: P[w] =
+// (A[16w+l], B[16w+l]), unscaled (x16).  `tile` is the slot's 2 KB tile.
+__device__ __forceinline__ void rotate_pair(f2 (&P)[16], uint32_t tile, int l) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) seq2(P[4 * j], P[4 * j + 1], P[4 * j + 2], P[4 * j + 3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) seq2(P[j], P[j + 4], P[j + 8], P[j + 12]);
+    // row l <- P (128 bytes, 16-byte chunk c at c ^ (l & 7)); then read column l
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        float a0, b0, a1, b1;
+        un2(P[2 * c], a0, b0);
+        un2(P[2 * c + 1], a1, b1);
+        st_shared_v4(tile + l * 128 + ((c ^ (l & 7)) << 4), __float_as_uint(a0), __float_as_uint(b0),
+                     __float_as_uint(a1), __float_as_uint(b1));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+        const uint32_t addr = tile + w * 128 + ((((l >> 1) ^ w) & 7) << 4) + ((l & 1) << 3);
+        asm volatile("ld.shared.b64 %0, [%1];" : "=l"(P[w].v) : "r"(addr));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly2(P[4 * j], P[4 * j + 1], P[4 * j + 2], P[4 * j + 3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly2(P[j], P[j + 4], P[j + 8], P[j + 12]);
+}
+
+__device__ __forceinline__ float halfwarp_max(float v) {
+#pragma unroll
+    for (int m = 8; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+template <int MODE, int ACT, int PPS>
+__global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
+    constexpr bool QUANT = (MODE == 0);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t s0 = smem_u32(smem);
+    const uint32_t in_base = s0;
+    const uint32_t out_base = in_base + p.ns * p.in_stage_bytes;
+    const uint32_t tile_base = out_base + 2 * p.out_stage_bytes;
+    unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - s0) + kSlots * kTileBytes);
+    uint64_t *fullb = reinterpret_cast<uint64_t *>(row_amax + 3 * 32);
+    const uint32_t full0 = smem_u32(fullb);
+    int *fault = &g_rot_fault;
+
+    const int slot = threadIdx.x >> 4, l = threadIdx.x & 15;
+    const uint32_t tile = tile_base + slot * kTileBytes;
+    const int groups = p.R * p.G;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.ns; ++s) mbar_init(full0 + 8 * s, 1);
+        fence_mbar_init();
+    }
+    if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
+    __syncthreads();
+
+    auto batch_rows = [&](int b) -> int {
+        const int64_t r0 = static_cast<int64_t>(b) * p.R;
+        const int64_t left = p.M - r0;
+        return static_cast<int>(left < p.R ? left : p.R);
+    };
+    auto issue = [&](int k) {  // batch k of this CTA into stage k % ns
+        const int b = blockIdx.x + k * gridDim.x;
+        if (b >= p.nbatch) return false;
+        const uint32_t bytes = batch_rows(b) * p.in_row_bytes;
+        const uint32_t bar = full0 + 8 * (k % p.ns);
+        mbar_expect_tx(bar, bytes);
+        bulk_load(in_base + (k % p.ns) * p.in_stage_bytes,
+                  p.in + static_cast<int64_t>(b) * p.R * p.in_row_bytes, bytes, bar);
+        return true;
+    };
+    int issued = 0;
+    if (threadIdx.x == 0)
+        for (int k = 0; k < p.ns; ++k) issued += issue(k) ? 1 : 0;
+
+    int k = 0;
+    for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
+        const int st = k % p.ns;
+        const int rows = batch_rows(b);
+        const int64_t row0 = static_cast<int64_t>(b) * p.R;
+        // every thread waits (acquiring the copy), and the CTA leaves together
+        // if any wait gave up
+        const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
+        if (!__syncthreads_and(ok)) break;
+        const uint32_t stage = in_base + st * p.in_stage_bytes;
+        unsigned int *amax_now = row_amax + 32 * (k % 3);
+
+        f2 vals[PPS][16];
+#pragma unroll
+        for (int j = 0; j < PPS; ++j) {
+            const int f0 = 2 * (slot + kSlots * j), f1 = f0 + 1;
+            const int r0 = f0 / p.G, g0 = f0 - r0 * p.G;
+            const int r1 = f1 / p.G, g1 = f1 - r1 * p.G;
+            const bool v0 = f0 < groups && r0 < rows, v1 = f1 < groups && r1 < rows;
+            float a[16], c[16];
+            if (v0) {
+                if constexpr (MODE == 3) {
+                    BulkParams q = p;
+                    q.row_scale = p.row_scale + row0;
+                    load16<MODE, ACT>(q, stage, r0, g0, l, a);
+                } else {
+                    load16<MODE, ACT>(p, stage, r0, g0, l, a);
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < 16; ++t) a[t] = 0.f;
+            }
+            if (v1) {
+                if constexpr (MODE == 3) {
+                    BulkParams q = p;
+                    q.row_scale = p.row_scale + row0;
+                    load16<MODE, ACT>(q, stage, r1, g1, l, c);
+                } else {
+                    load16<MODE, ACT>(p, stage, r1, g1, l, c);
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < 16; ++t) c[t] = 0.f;
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) vals[j][t] = mk2(a[t], c[t]);
+            rotate_pair(vals[j], tile, l);
+            if constexpr (QUANT) {
+                float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    float x0, x1;
+                    un2(vals[j][t], x0, x1);
+                    m0 = fmaxf(m0, fabsf(x0));
+                    m1 = fmaxf(m1, fabsf(x1));
+                }
+                m0 = halfwarp_max(m0);
+                m1 = halfwarp_max(m1);
+                if (l == 0) {
+                    if (v0) atomicMax(amax_now + r0, __float_as_uint(m0));
+                    if (v1) atomicMax(amax_now + r1, __float_as_uint(m1));
+                }
+            }
+        }
+        if constexpr (QUANT) {
+            if (threadIdx.x < 32) row_amax[32 * ((k + 1) % 3) + threadIdx.x] = 0u;
+        }
+        if (threadIdx.x == 0) bulk_wait_read<1>();  // out stage k&1 is free again
+        __syncthreads();
+        if (threadIdx.x == 0 && issue(k + p.ns)) ++issued;
+
+        const uint32_t ostage = out_base + (k & 1) * p.out_stage_bytes;
+#pragma unroll
+        for (int j = 0; j < PPS; ++j) {
+            const int f0 = 2 * (slot + kSlots * j), f1 = f0 + 1;
+            const int r0 = f0 / p.G, g0 = f0 - r0 * p.G;
+            const int r1 = f1 / p.G, g1 = f1 - r1 * p.G;
+            const bool v0 = f0 < groups && r0 < rows, v1 = f1 < groups && r1 < rows;
+            if constexpr (QUANT) {
+                float inv0 = 0.f, inv1 = 0.f;
+                if (v0) {
+                    const float s = fmaxf(__fdiv_rn(__fmul_rn(__uint_as_float(amax_now[r0]), 0.0625f), 127.0f), 1e-30f);
+                    inv0 = __fmul_rn(__frcp_rn(s), 0.0625f);
+                    if (g0 == 0 && l == 0) p.scale[row0 + r0] = s;
+                }
+                if (v1) {
+                    const float s = fmaxf(__fdiv_rn(__fmul_rn(__uint_as_float(amax_now[r1]), 0.0625f), 127.0f), 1e-30f);
+                    inv1 = __fmul_rn(__frcp_rn(s), 0.0625f);
+                    if (g1 == 0 && l == 0) p.scale[row0 + r1] = s;
+                }
+                const f2 inv = mk2(inv0, inv1);
+                const f2 magic = mk2(12582912.0f, 12582912.0f);
+                const uint32_t o0 = ostage + r0 * p.out_row_bytes + g0 * 256 + l;
+                const uint32_t o1 = ostage + r1 * p.out_row_bytes + g1 * 256 + l;
+#pragma unroll
+                for (int w = 0; w < 16; ++w) {
+                    // rint(v * (1/s)): |v/s| <= 127 (+ulps), so the low byte of
+                    // (v/s + 1.5*2^23) is the two's-complement code
+                    float q0, q1;
+                    un2(add2(mul2(vals[j][w], inv), magic), q0, q1);
+                    if (v0) asm volatile("st.shared.u8 [%0], %1;" ::"r"(o0 + 16 * w), "r"(__float_as_uint(q0)) : "memory");
+                    if (v1) asm volatile("st.shared.u8 [%0], %1;" ::"r"(o1 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
+                }
+            } else {
+                const f2 sixteenth = mk2(0.0625f, 0.0625f);
+                const uint32_t o0 = ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2;
+                const uint32_t o1 = ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2;
+#pragma unroll
+                for (int w = 0; w < 16; ++w) {
+                    float x0, x1;
+                    un2(mul2(vals[j][w], sixteenth), x0, x1);
+                    const uint32_t hb = cvt_bf16x2(x0, x1);
+                    if (v0) asm volatile("st.shared.u16 [%0], %1;" ::"r"(o0 + 32 * w), "r"(hb & 0xFFFFu) : "memory");
+                    if (v1) asm volatile("st.shared.u16 [%0], %1;" ::"r"(o1 + 32 * w), "r"(hb >> 16) : "memory");
+                }
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store(p.out + row0 * p.out_row_bytes, ostage, rows * p.out_row_bytes);
+            bulk_commit();
+        }
+    }
+    if (threadIdx.x == 0) {
+        // batches whose copies were issued but not consumed (after a fault)
+        for (int kk = k; kk < issued; ++kk) {
+            const uint32_t bar = full0 + 8 * (kk % p.ns);
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(bar, (kk / p.ns) & 1))
+                if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+        }
+        bulk_wait<0>();
+    }
+    __syncthreads();
+}
+
+template <int MODE, int ACT>
+int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
+    auto pick = [&](auto kern) -> int {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)) != cudaSuccess)
+            return launch_status("rotate (shared memory attribute)");
+        // resident blocks per SM for this kernel and shared-memory size (cached)
+        static size_t cached_smem = 0;
+        static int cached_per_sm = 0;
+        if (cached_smem != smem) {
+            int per = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess)
+                per = 1;
+            cached_per_sm = std::max(1, per);
+            cached_smem = smem;
+        }
+        const int per_sm = cached_per_sm;
+        const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * per_sm);
+        kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
+        return launch_status("rotate");
+    };
+    switch (pps) {
+        case 1: return pick(rotate_bulk_kernel<MODE, ACT, 1>);
+        case 2: return pick(rotate_bulk_kernel<MODE, ACT, 2>);
+        case 4: return pick(rotate_bulk_kernel<MODE, ACT, 4>);
+        default: break;
+    }
+    set_error("unsupported group count per slot");
+    return 4;
+}
+
+}  // namespace
+
+// Returns -1 when the shape does not fit the streaming kernel (the caller then
+// uses the register-staged kernel of rotate.cu).
+int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
+                       void *out, float *scale, int64_t M, int64_t K) {
+    const int64_t G = K / kGroup;
+    int pps = 0, R = 0;
+    double best = -1;
+    for (int c : {1, 2, 4}) {
+        if (G > 2 * kSlots * c) continue;
+        const int r = static_cast<int>((2 * kSlots * c) / G);
+        const double util = static_cast<double>(r * G) / (2 * kSlots * c);
+        if (util >= 0.85) { pps = c; R = r; break; }
+        if (util > best) { best = util; pps = c; R = r; }
+    }
+    if (pps == 0 || R < 1) return -1;
+    if (R > 32) R = 32;
+    BulkParams p{};
+    p.in = static_cast<const uint8_t *>(in);
+    p.row_scale = row_scale;
+    p.out = static_cast<uint8_t *>(out);
+    p.scale = scale;
+    p.M = M; p.K = K; p.G = static_cast<int>(G); p.R = R;
+    const bool paired = mode == 0 && act_paired(act);
+    p.in_row_bytes = static_cast<uint32_t>(mode == 3 ? K : (paired ? 4 * K : 2 * K));
+    p.out_row_bytes = static_cast<uint32_t>(mode == 0 ? K : 2 * K);
+    auto up = [](uint32_t x) { return (x + 127u) & ~127u; };
+    p.in_stage_bytes = up(R * p.in_row_bytes);
+    p.out_stage_bytes = up(R * p.out_row_bytes);
+    const int64_t nb = (M + R - 1) / R;
+    if (nb > 0x7FFFFFFF) return -1;
+    p.nbatch = static_cast<int>(nb);
+    p.ns = 3;
+    auto total = [&](int ns) {
+        return static_cast<size_t>(ns) * p.in_stage_bytes + 2 * p.out_stage_bytes +
+               kSlots * kTileBytes + 3 * 32 * 4 + 8 * ns;
+    };
+    if (total(3) > 200 * 1024) p.ns = 2;
+    if (total(p.ns) > 200 * 1024) return -1;
+    const size_t smem = total(p.ns);
+    if (mode == 0) {
+        switch (act) {
+            case 0: return launch_pps<0, 0>(s, p, pps, smem);
+            case 1: return launch_pps<0, 1>(s, p, pps, smem);
+            case 2: return launch_pps<0, 2>(s, p, pps, smem);
+            case 3: return launch_pps<0, 3>(s, p, pps, smem);
+            case 4: return launch_pps<0, 4>(s, p, pps, smem);
+            case 5: return launch_pps<0, 5>(s, p, pps, smem);
+            default: return -1;
+        }
+    }
+    if (mode == 2) return launch_pps<2, 0>(s, p, pps, smem);
+    if (mode == 3) return launch_pps<3, 0>(s, p, pps, smem);
+    return -1;
+}
+
+int rot_fault_status(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_rot_fault, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_rot_fault, &zero, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace xpuint8

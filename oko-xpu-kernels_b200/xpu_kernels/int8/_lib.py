@@ -73,7 +73,7 @@ def _signatures():
         "xpuint8_int_mm_geglu_stream": [vp] * 6 + [i64] * 3,
         "xpuint8_linear_stream": [vp] * 8 + [i64] * 3 + [i32],
         "xpuint8_ffn_workspace_bytes": [i64, i64, i64, i32],
-        "xpuint8_ffn_stream": [vp] * 10 + [i64] * 3 + [i32],
+        "xpuint8_ffn_stream": [vp] * 9 + [i64] * 3 + [i32],
         "xpuint8_quantize_row_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_colquant_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_fault_status": [i32],

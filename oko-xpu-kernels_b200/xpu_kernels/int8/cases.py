@@ -1,0 +1,176 @@
+"""Run one kernel of the library on one shape, for profiling and quick timing.
+
+    python -m xpu_kernels.int8.cases gemm --M 2048 --N 10240 --K 1280 --iters 20
+    python -m xpu_kernels.int8.cases rotate_quant --M 65536 --K 4096
+    python -m xpu_kernels.int8.cases linear | ffn | dx | dw | quantize_row | dequant
+
+Inputs are seeded and generated on the device; each case launches its kernel
+`--iters` times over `--sets` rotating buffer sets and prints the average
+device time per launch (CUDA events) with the algorithmic throughput.  It is
+the driver the committed ncu summaries name (profile one launch with
+``ncu -k regex:<kernel> -s <skip> -c 1``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import ops
+from ._lib import _lib, _ptr, _stream
+
+
+def _time(fn, iters, stream):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(min(3, iters)):
+        fn(i)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(iters):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["gemm", "gemm_raw", "gemm_nn", "gemm_tn", "geglu",
+                                     "rotate_quant", "rotate", "linear", "ffn", "dx", "dw",
+                                     "quantize_row", "dequant", "dequant_act"])
+    ap.add_argument("--M", type=int, default=2048)
+    ap.add_argument("--N", type=int, default=10240)
+    ap.add_argument("--K", type=int, default=1280)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--sets", type=int, default=2)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib()
+    st = torch.cuda.current_stream(dev)
+    sp = _stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    M, N, K = a.M, a.N, a.K
+
+    def i8(*shape):
+        return torch.randint(-127, 128, shape, generator=g, device=dev, dtype=torch.int8)
+
+    def bf(*shape, s=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * s).to(torch.bfloat16)
+
+    def f32(*shape):
+        return torch.rand(*shape, generator=g, device=dev) * 1e-3 + 1e-5
+
+    S = a.sets
+    if a.case in ("gemm", "gemm_raw", "gemm_nn", "gemm_tn", "geglu"):
+        lay = {"gemm": 0, "gemm_raw": 0, "gemm_nn": 1, "gemm_tn": 2, "geglu": 0}[a.case]
+        nb = 2 * N if a.case == "geglu" else N
+        A = [i8(M, K) if lay < 2 else i8(K, M) for _ in range(S)]
+        B = [i8(nb, K) if lay == 0 else i8(K, N) for _ in range(S)]
+        xs, ws, bias = f32(M), f32(nb), f32(N)
+        if a.case == "gemm_raw":
+            O = [torch.empty(M, N, dtype=torch.int32, device=dev) for _ in range(S)]
+        else:
+            O = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for _ in range(S)]
+
+        def fn(i):
+            j = i % S
+            if a.case == "gemm_raw":
+                rc = lib.xpuint8_int_mm_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]), M, N, K, 0, N)
+            elif a.case == "geglu":
+                rc = lib.xpuint8_int_mm_geglu_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
+                                                     _ptr(xs), _ptr(ws), M, N, K)
+            else:
+                rc = lib.xpuint8_int_mm_dequant_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
+                                                       _ptr(xs), _ptr(ws), _ptr(bias), M, N, K,
+                                                       lay, N)
+            assert rc == 0, lib.xpuint8_last_error()
+        ops_ = 2.0 * M * (2 * N if a.case == "geglu" else N) * K
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "TOPS": ops_ / (t * 1e-3) / 1e12}
+    elif a.case in ("rotate_quant", "rotate", "quantize_row"):
+        X = [bf(M, K) for _ in range(S)]
+        Q = [torch.empty(M, K, dtype=torch.bfloat16 if a.case == "rotate" else torch.int8,
+                         device=dev) for _ in range(S)]
+        sc = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(S)]
+
+        def fn(i):
+            j = i % S
+            if a.case == "rotate_quant":
+                rc = lib.xpuint8_convrot_quantize_stream(sp, _ptr(X[j]), _ptr(Q[j]), _ptr(sc[j]), M, K)
+            elif a.case == "rotate":
+                rc = lib.xpuint8_convrot_rotate_bf16_stream(sp, _ptr(X[j]), _ptr(Q[j]), M, K)
+            else:
+                rc = lib.xpuint8_quantize_row_stream(sp, _ptr(X[j]), None, _ptr(Q[j]), _ptr(sc[j]), M, K)
+            assert rc == 0, lib.xpuint8_last_error()
+        nbytes = (4 * M * K) if a.case == "rotate" else (3 * M * K + 4 * M)
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9, "bytes": nbytes}
+    elif a.case == "dequant":
+        ACC = [torch.randint(-2 ** 20, 2 ** 20, (M, N), generator=g, device=dev, dtype=torch.int32)
+               for _ in range(S)]
+        O = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for _ in range(S)]
+        xs, ws, bias = f32(M), f32(N), f32(N)
+
+        def fn(i):
+            j = i % S
+            rc = lib.xpuint8_dequant_epilogue_stream(sp, _ptr(ACC[j]), _ptr(O[j]), _ptr(xs), _ptr(ws),
+                                                     _ptr(bias), M, N)
+            assert rc == 0, lib.xpuint8_last_error()
+        nbytes = 6 * M * N + 4 * M + 12 * N
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9}
+    elif a.case == "dequant_act":
+        ACC = [torch.randint(-2 ** 20, 2 ** 20, (M, 2 * K), generator=g, device=dev,
+                             dtype=torch.int32) for _ in range(S)]
+        Q = [torch.empty(M, K, dtype=torch.int8, device=dev) for _ in range(S)]
+        sc = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(S)]
+        xs, ws = f32(M), f32(2 * K)
+
+        def fn(i):
+            j = i % S
+            rc = lib.xpuint8_dequant_act_quantize_stream(sp, _ptr(ACC[j]), _ptr(Q[j]), _ptr(sc[j]),
+                                                         _ptr(xs), _ptr(ws), M, K, 4)
+            assert rc == 0, lib.xpuint8_last_error()
+        nbytes = 8 * M * K + 8 * K + M * K + 8 * M
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9}
+    elif a.case == "linear":
+        X = [bf(M, K) for _ in range(S)]
+        w8, ws = ops.prepare_weight(bf(N, K, s=0.02))
+
+        def fn(i):
+            ops.linear(X[i % S], w8, ws)
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "TOPS": 2.0 * M * N * K / (t * 1e-3) / 1e12}
+    elif a.case == "ffn":
+        inner = N // 2
+        X = [bf(M, K) for _ in range(S)]
+        up8, ups = ops.prepare_weight(bf(N, K, s=0.02))
+        dn8, dns = ops.prepare_weight(bf(K, inner, s=0.02))
+
+        def fn(i):
+            ops.ffn(X[i % S], up8, ups, dn8, dns, act="geglu_erf")
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t,
+               "TOPS": (2.0 * M * N * K + 2.0 * M * inner * K) / (t * 1e-3) / 1e12}
+    elif a.case in ("dx", "dw"):
+        x = bf(M, K)
+        w8, ws = ops.prepare_weight(bf(N, K, s=0.02))
+        dy = bf(M, N, s=1e-3)
+        xq, xs = ops.quantize(x)
+
+        def fn(i):
+            if a.case == "dx":
+                ops.linear_dx_int8(dy, w8, ws)
+            else:
+                ops.linear_dw_int8(dy, xq, xs)
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "TOPS": 2.0 * M * N * K / (t * 1e-3) / 1e12}
+    res.update({"M": M, "N": N, "K": K})
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()
