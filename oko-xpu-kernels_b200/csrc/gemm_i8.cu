@@ -161,18 +161,21 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmO
             for (int j = 0; j < 32; j += 4) {
                 const float4 w = *reinterpret_cast<const float4 *>(s_ws + c * 32 + j);
                 const float4 b = *reinterpret_cast<const float4 *>(s_b + c * 32 + j);
-                // float(acc) * (w_scale[n] * x_scale[m]) + bias[n], each op rounded
-                f2 s01 = mul2(mk2(w.x, w.y), xs2), s23 = mul2(mk2(w.z, w.w), xs2);
-                f2 p01 = mul2(mk2(static_cast<float>(static_cast<int32_t>(r[j])),
-                                  static_cast<float>(static_cast<int32_t>(r[j + 1]))), s01);
-                f2 p23 = mul2(mk2(static_cast<float>(static_cast<int32_t>(r[j + 2])),
-                                  static_cast<float>(static_cast<int32_t>(r[j + 3]))), s23);
+                // float(acc) * (w_scale[n] * x_scale[m]) + bias[n], each op rounded.
+                // The product feeding the bias add is a scalar __fmul_rn: ptxas
+                // contracts a packed f32x2 multiply followed by a packed add.
+                float s[4];
+                un2(mul2(mk2(w.x, w.y), xs2), s[0], s[1]);
+                un2(mul2(mk2(w.z, w.w), xs2), s[2], s[3]);
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    v[j + t] = __fmul_rn(static_cast<float>(static_cast<int32_t>(r[j + t])), s[t]);
                 if (a.bias) {
-                    p01 = add2(p01, mk2(b.x, b.y));
-                    p23 = add2(p23, mk2(b.z, b.w));
+                    f2 p01 = add2(mk2(v[j], v[j + 1]), mk2(b.x, b.y));
+                    f2 p23 = add2(mk2(v[j + 2], v[j + 3]), mk2(b.z, b.w));
+                    un2(p01, v[j], v[j + 1]);
+                    un2(p23, v[j + 2], v[j + 3]);
                 }
-                un2(p01, v[j], v[j + 1]);
-                un2(p23, v[j + 2], v[j + 3]);
             }
             stage_reserve(lane);
             const uint32_t buf = bufs + bsel * kStageBytes;

@@ -44,6 +44,7 @@ namespace {
 
 constexpr int kSlots = 16;             // half-warps per 256-thread CTA
 constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
+constexpr int kScratch = 512;          // behind each output stage: sink for invalid groups
 
 struct BulkParams {
     const uint8_t *in;
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
     const uint32_t s0 = smem_u32(smem);
     const uint32_t in_base = s0;
     const uint32_t out_base = in_base + p.ns * p.in_stage_bytes;
-    const uint32_t tile_base = out_base + 2 * p.out_stage_bytes;
+    const uint32_t tile_base = out_base + 2 * (p.out_stage_bytes + kScratch);
     unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - s0) + kSlots * kTileBytes);
     uint64_t *fullb = reinterpret_cast<uint64_t *>(row_amax + 3 * 32);
     const uint32_t full0 = smem_u32(fullb);
@@ -222,6 +223,9 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         for (int k = 0; k < p.ns; ++k) issued += issue(k) ? 1 : 0;
 
     int k = 0;
+    int64_t pend_row0 = 0;
+    int pend_rows = 0;
+    uint32_t pend_stage = 0;
     for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
         const int st = k % p.ns;
         const int rows = batch_rows(b);
@@ -230,6 +234,12 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         // if any wait gave up
         const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
         if (!__syncthreads_and(ok)) break;
+        // the previous batch's output stage is complete: send it
+        if (threadIdx.x == 0 && pend_rows > 0) {
+            bulk_store(p.out + pend_row0 * p.out_row_bytes, pend_stage, pend_rows * p.out_row_bytes);
+            bulk_commit();
+        }
+        pend_rows = 0;
         const uint32_t stage = in_base + st * p.in_stage_bytes;
         unsigned int *amax_now = row_amax + 32 * (k % 3);
 
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         __syncthreads();
         if (threadIdx.x == 0 && issue(k + p.ns)) ++issued;
 
-        const uint32_t ostage = out_base + (k & 1) * p.out_stage_bytes;
+        const uint32_t ostage = out_base + (k & 1) * (p.out_stage_bytes + kScratch);
 #pragma unroll
         for (int j = 0; j < PPS; ++j) {
             const int f0 = 2 * (slot + kSlots * j), f1 = f0 + 1;
@@ -311,39 +321,48 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
                     inv1 = __fmul_rn(__frcp_rn(s), 0.0625f);
                     if (g1 == 0 && l == 0) p.scale[row0 + r1] = s;
                 }
-                const f2 inv = mk2(inv0, inv1);
                 const f2 magic = mk2(12582912.0f, 12582912.0f);
-                const uint32_t o0 = ostage + r0 * p.out_row_bytes + g0 * 256 + l;
-                const uint32_t o1 = ostage + r1 * p.out_row_bytes + g1 * 256 + l;
+                // an invalid group of a pair writes into a scratch row of the
+                // stage (never stored), so the loop has no per-element branch
+                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + g0 * 256 + l : ostage + p.out_stage_bytes;
+                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + g1 * 256 + l : ostage + p.out_stage_bytes;
 #pragma unroll
                 for (int w = 0; w < 16; ++w) {
                     // rint(v * (1/s)): |v/s| <= 127 (+ulps), so the low byte of
-                    // (v/s + 1.5*2^23) is the two's-complement code
-                    float q0, q1;
-                    un2(add2(mul2(vals[j][w], inv), magic), q0, q1);
-                    if (v0) asm volatile("st.shared.u8 [%0], %1;" ::"r"(o0 + 16 * w), "r"(__float_as_uint(q0)) : "memory");
-                    if (v1) asm volatile("st.shared.u8 [%0], %1;" ::"r"(o1 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
+                    // (v/s + 1.5*2^23) is the two's-complement code.  The
+                    // products are scalar __fmul_rn: ptxas contracts a packed
+                    // f32x2 multiply feeding a packed add into one FFMA2, which
+                    // would round v*(1/s) + 1.5*2^23 once instead of twice.
+                    float x0, x1, q0, q1;
+                    un2(vals[j][w], x0, x1);
+                    un2(add2(mk2(__fmul_rn(x0, inv0), __fmul_rn(x1, inv1)), magic), q0, q1);
+                    asm volatile("st.shared.u8 [%0], %1;" ::"r"(o0 + 16 * w), "r"(__float_as_uint(q0)) : "memory");
+                    asm volatile("st.shared.u8 [%0], %1;" ::"r"(o1 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
                 }
             } else {
                 const f2 sixteenth = mk2(0.0625f, 0.0625f);
-                const uint32_t o0 = ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2;
-                const uint32_t o1 = ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2;
+                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2 : ostage + p.out_stage_bytes;
+                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2 : ostage + p.out_stage_bytes;
 #pragma unroll
                 for (int w = 0; w < 16; ++w) {
                     float x0, x1;
                     un2(mul2(vals[j][w], sixteenth), x0, x1);
                     const uint32_t hb = cvt_bf16x2(x0, x1);
-                    if (v0) asm volatile("st.shared.u16 [%0], %1;" ::"r"(o0 + 32 * w), "r"(hb & 0xFFFFu) : "memory");
-                    if (v1) asm volatile("st.shared.u16 [%0], %1;" ::"r"(o1 + 32 * w), "r"(hb >> 16) : "memory");
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(o0 + 32 * w), "r"(hb & 0xFFFFu) : "memory");
+                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(o1 + 32 * w), "r"(hb >> 16) : "memory");
                 }
             }
         }
+        // the stage is handed to the copy engine after the next barrier
         fence_async_smem();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            bulk_store(p.out + row0 * p.out_row_bytes, ostage, rows * p.out_row_bytes);
-            bulk_commit();
-        }
+        pend_row0 = row0;
+        pend_rows = rows;
+        pend_stage = ostage;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && pend_rows > 0) {
+        bulk_store(p.out + pend_row0 * p.out_row_bytes, pend_stage, pend_rows * p.out_row_bytes);
+        bulk_commit();
     }
     if (threadIdx.x == 0) {
         // batches whose copies were issued but not consumed (after a fault)
@@ -424,7 +443,7 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     p.nbatch = static_cast<int>(nb);
     p.ns = 3;
     auto total = [&](int ns) {
-        return static_cast<size_t>(ns) * p.in_stage_bytes + 2 * p.out_stage_bytes +
+        return static_cast<size_t>(ns) * p.in_stage_bytes + 2 * (p.out_stage_bytes + kScratch) +
                kSlots * kTileBytes + 3 * 32 * 4 + 8 * ns;
     };
     if (total(3) > 200 * 1024) p.ns = 2;
