@@ -53,7 +53,7 @@ constexpr int kThreads = 192;
 constexpr int kTmemCols = 2 * BN;
 constexpr int GROUP_M = 16;
 constexpr size_t kSmemBytes =
-    static_cast<size_t>(STAGES) * STAGE_BYTES + 4 * 2 * 32 * 64 + 2 * BN * 4 + 1024 + 256;
+    static_cast<size_t>(STAGES) * STAGE_BYTES + 4 * 3 * 32 * 64 + 2 * BN * 4 + 1024 + 256;
 
 struct GemmArgs {
     void *out;
@@ -86,14 +86,15 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     atomicCAS(&g_gemm_fault, 0, 99);
 }
 
-// Epilogue staging.  Each epilogue warp owns two 2 KB buffers of 32 rows x 64
+// Epilogue staging.  Each epilogue warp owns three 2 KB buffers of 32 rows x 64
 // bytes (64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r>>1)&3),
 // the pattern the TMA store unswizzles).  A 32-column chunk of the warp's 32
 // rows (bf16; int32 uses 16-column chunks) is converted in registers, written
 // to one buffer and handed to a TMA bulk-tensor store, which also clips the
-// M/N tails; the other buffer is filled meanwhile.
+// M/N tails; the next buffers are filled meanwhile.
 constexpr int kStageBytes = 32 * 64;
-constexpr int kEpiSmem = 4 * 2 * kStageBytes;  // 4 warps x 2 buffers
+constexpr int kStageBufs = 3;                           // per epilogue warp
+constexpr int kEpiSmem = 4 * kStageBufs * kStageBytes;  // 4 warps
 
 __device__ __forceinline__ uint32_t stage_chunk_addr(uint32_t buf, int row, int c) {
     return buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4);
@@ -117,109 +118,122 @@ __device__ __forceinline__ void stage_flush(const void *tmap, uint32_t buf, int 
         bulk_commit();
     }
 }
-// before refilling a buffer: its previous store must have read it
+// before refilling a buffer: its previous store (kStageBufs stores ago) must
+// have read it
 __device__ __forceinline__ void stage_reserve(int lane) {
-    if (lane == 0) bulk_wait_read<1>();
+    if (lane == 0) bulk_wait_read<kStageBufs - 1>();
     __syncwarp();
 }
 
+// dequant of 32 accumulators of one row: float(acc) * (w_scale[n] * x_scale[m])
+// (+ bias[n]), each operation rounded.  The product feeding the bias add is a
+// scalar __fmul_rn: ptxas contracts a packed f32x2 multiply followed by a
+// packed add into one FFMA2.
+__device__ __forceinline__ void dequant32(const uint32_t (&r)[32], const float *ws, const float *bs,
+                                          f2 xs2, bool bias, float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 w = *reinterpret_cast<const float4 *>(ws + j);
+        float s[4];
+        un2(mul2(mk2(w.x, w.y), xs2), s[0], s[1]);
+        un2(mul2(mk2(w.z, w.w), xs2), s[2], s[3]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+            v[j + t] = __fmul_rn(static_cast<float>(static_cast<int32_t>(r[j + t])), s[t]);
+        if (bias) {
+            const float4 b = *reinterpret_cast<const float4 *>(bs + j);
+            f2 p01 = add2(mk2(v[j], v[j + 1]), mk2(b.x, b.y));
+            f2 p23 = add2(mk2(v[j + 2], v[j + 3]), mk2(b.z, b.w));
+            un2(p01, v[j], v[j + 1]);
+            un2(p23, v[j + 2], v[j + 3]);
+        }
+    }
+}
+
+// y = bf16(h * bf16(gelu_erf(g))) from the hidden and gate accumulators
+__device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t (&rg)[32],
+                                        const float *wsh, const float *wsg, f2 xs2, float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        const float2 wh = *reinterpret_cast<const float2 *>(wsh + j);
+        const float2 wg = *reinterpret_cast<const float2 *>(wsg + j);
+        float h0, h1, g0, g1;
+        un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rh[j])),
+                     static_cast<float>(static_cast<int32_t>(rh[j + 1]))),
+                 mul2(mk2(wh.x, wh.y), xs2)), h0, h1);
+        un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rg[j])),
+                     static_cast<float>(static_cast<int32_t>(rg[j + 1]))),
+                 mul2(mk2(wg.x, wg.y), xs2)), g0, g1);
+        // h, g rounded to bf16 (the unfused chain stores them), then
+        // y = bf16(h * bf16(0.5 g (1 + erf(g / sqrt 2))))
+        h0 = round_bf16(h0); h1 = round_bf16(h1);
+        g0 = round_bf16(g0); g1 = round_bf16(g1);
+        const float e0 = __fmul_rn(__fmul_rn(0.5f, g0),
+                                   __fadd_rn(1.0f, erff(__fmul_rn(g0, 0.7071067811865476f))));
+        const float e1 = __fmul_rn(__fmul_rn(0.5f, g1),
+                                   __fadd_rn(1.0f, erff(__fmul_rn(g1, 0.7071067811865476f))));
+        v[j] = __fmul_rn(h0, round_bf16(e0));
+        v[j + 1] = __fmul_rn(h1, round_bf16(e1));
+    }
+}
+
+// Drain one accumulator tile.  TMEM loads are software-pipelined: the load of
+// chunk c+1 is in flight while chunk c is converted and staged.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmOut, uint32_t taddr,
                                               int m0, int n0, int quarter, int lane, float xs,
                                               const float *s_ws, const float *s_b, uint32_t bufs,
                                               int &bsel) {
     const int y = m0 + quarter * 32;
-    if constexpr (EPI == kEpiRawI32) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            if (n0 + c * 32 >= a.N) break;
-            uint32_t r[32];
-            tmem_ld32(taddr + c * 32, r);
-            tmem_wait_ld();
+    constexpr int NCH = (EPI == kEpiGegluBf16) ? 4 : BN / 32;  // 32-column chunks
+    const int nch = min(NCH, (a.N - n0 + 31) / 32);
+    const f2 xs2 = mk2(xs, xs);
+    const bool bias = a.bias != nullptr;
+    uint32_t ra[32], rb[32], ga[32], gb[32];
+    // chunk 0
+    tmem_ld32(taddr, ra);
+    if constexpr (EPI == kEpiGegluBf16) tmem_ld32(taddr + 128, ga);
+    tmem_wait_ld(ra);
+    if constexpr (EPI == kEpiGegluBf16) tmem_wait_ld(ga);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        if (c >= nch) break;
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        uint32_t(&gcur)[32] = (c & 1) ? gb : ga;
+        uint32_t(&gnxt)[32] = (c & 1) ? ga : gb;
+        if (c + 1 < nch) {
+            tmem_ld32(taddr + (c + 1) * 32, nxt);
+            if constexpr (EPI == kEpiGegluBf16) tmem_ld32(taddr + 128 + (c + 1) * 32, gnxt);
+        }
+        if constexpr (EPI == kEpiRawI32) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 stage_reserve(lane);
                 const uint32_t buf = bufs + bsel * kStageBytes;
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    st_shared_v4(stage_chunk_addr(buf, lane, q), r[16 * h + 4 * q], r[16 * h + 4 * q + 1],
-                                 r[16 * h + 4 * q + 2], r[16 * h + 4 * q + 3]);
+                    st_shared_v4(stage_chunk_addr(buf, lane, q), cur[16 * h + 4 * q],
+                                 cur[16 * h + 4 * q + 1], cur[16 * h + 4 * q + 2],
+                                 cur[16 * h + 4 * q + 3]);
                 stage_flush(tmOut, buf, lane, n0 + c * 32 + 16 * h, y);
-                bsel ^= 1;
+                bsel = bsel + 1 == kStageBufs ? 0 : bsel + 1;
             }
-        }
-    } else if constexpr (EPI == kEpiDequantBf16) {
-        const f2 xs2 = mk2(xs, xs);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            if (n0 + c * 32 >= a.N) break;
-            uint32_t r[32];
-            tmem_ld32(taddr + c * 32, r);
-            tmem_wait_ld();
+        } else {
             float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 w = *reinterpret_cast<const float4 *>(s_ws + c * 32 + j);
-                const float4 b = *reinterpret_cast<const float4 *>(s_b + c * 32 + j);
-                // float(acc) * (w_scale[n] * x_scale[m]) + bias[n], each op rounded.
-                // The product feeding the bias add is a scalar __fmul_rn: ptxas
-                // contracts a packed f32x2 multiply followed by a packed add.
-                float s[4];
-                un2(mul2(mk2(w.x, w.y), xs2), s[0], s[1]);
-                un2(mul2(mk2(w.z, w.w), xs2), s[2], s[3]);
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    v[j + t] = __fmul_rn(static_cast<float>(static_cast<int32_t>(r[j + t])), s[t]);
-                if (a.bias) {
-                    f2 p01 = add2(mk2(v[j], v[j + 1]), mk2(b.x, b.y));
-                    f2 p23 = add2(mk2(v[j + 2], v[j + 3]), mk2(b.z, b.w));
-                    un2(p01, v[j], v[j + 1]);
-                    un2(p23, v[j + 2], v[j + 3]);
-                }
-            }
+            if constexpr (EPI == kEpiDequantBf16)
+                dequant32(cur, s_ws + c * 32, s_b + c * 32, xs2, bias, v);
+            else
+                geglu32(cur, gcur, s_ws + c * 32, s_ws + 128 + c * 32, xs2, v);
             stage_reserve(lane);
             const uint32_t buf = bufs + bsel * kStageBytes;
             stage_bf16_32(buf, lane, v);
             stage_flush(tmOut, buf, lane, n0 + c * 32, y);
-            bsel ^= 1;
+            bsel = bsel + 1 == kStageBufs ? 0 : bsel + 1;
         }
-    } else {  // GEGLU: hidden columns [0,128) and gate columns [128,256) of the accumulator
-        const f2 xs2 = mk2(xs, xs);
-#pragma unroll 1
-        for (int c = 0; c < 128 / 32; ++c) {
-            if (n0 + c * 32 >= a.N) break;
-            uint32_t rh[32], rg[32];
-            tmem_ld32(taddr + c * 32, rh);
-            tmem_ld32(taddr + 128 + c * 32, rg);
-            tmem_wait_ld();
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float2 wh = *reinterpret_cast<const float2 *>(s_ws + c * 32 + j);
-                const float2 wg = *reinterpret_cast<const float2 *>(s_ws + 128 + c * 32 + j);
-                float h0, h1, g0, g1;
-                un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rh[j])),
-                             static_cast<float>(static_cast<int32_t>(rh[j + 1]))),
-                         mul2(mk2(wh.x, wh.y), xs2)), h0, h1);
-                un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rg[j])),
-                             static_cast<float>(static_cast<int32_t>(rg[j + 1]))),
-                         mul2(mk2(wg.x, wg.y), xs2)), g0, g1);
-                // h, g rounded to bf16 (the unfused chain stores them), then
-                // y = bf16(h * bf16(0.5 g (1 + erf(g / sqrt 2))))
-                h0 = round_bf16(h0); h1 = round_bf16(h1);
-                g0 = round_bf16(g0); g1 = round_bf16(g1);
-                const float e0 = __fmul_rn(__fmul_rn(0.5f, g0),
-                                           __fadd_rn(1.0f, erff(__fmul_rn(g0, 0.7071067811865476f))));
-                const float e1 = __fmul_rn(__fmul_rn(0.5f, g1),
-                                           __fadd_rn(1.0f, erff(__fmul_rn(g1, 0.7071067811865476f))));
-                v[j] = __fmul_rn(h0, round_bf16(e0));
-                v[j + 1] = __fmul_rn(h1, round_bf16(e1));
-            }
-            stage_reserve(lane);
-            const uint32_t buf = bufs + bsel * kStageBytes;
-            stage_bf16_32(buf, lane, v);
-            stage_flush(tmOut, buf, lane, n0 + c * 32, y);
-            bsel ^= 1;
+        if (c + 1 < nch) {
+            tmem_wait_ld(nxt);
+            if constexpr (EPI == kEpiGegluBf16) tmem_wait_ld(gnxt);
         }
     }
 }
@@ -357,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------------- epilogue
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
         const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
-        const uint32_t bufs = sEpi + (warp - 2) * 2 * kStageBytes;
+        const uint32_t bufs = sEpi + (warp - 2) * kStageBufs * kStageBytes;
         int bsel = 0;
         int acc = 0;
         uint32_t aph = 0;
