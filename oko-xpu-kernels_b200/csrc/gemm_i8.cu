@@ -16,15 +16,16 @@
 //           and gate rows [N+n, N+n+128) into one 256-wide B tile, and writes
 //           y = bf16(h * bf16(gelu_erf(g))) with h, g the bf16-rounded dequants
 //
-// Structure (one CTA per SM, persistent over output tiles, 192 threads):
+// Structure (one CTA per SM, persistent over output tiles, 320 threads):
 //   warp 0     TMA producer (one thread): A 128x128 and B 256x128 int8 tiles per
 //              k-block into a 4-stage shared-memory ring (128-byte swizzle)
 //   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
 //              tcgen05.mma.kind::i8 (128x256x32) per k-block, tcgen05.commit to
 //              free the ring slot and, per tile, to hand the accumulator over
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time (warp w drains TMEM
-//              lanes 32*(w%4)..+31, i.e. one output row per thread), scale,
-//              convert and store
+//   warps 2-9  epilogue: tcgen05.ld 32 columns at a time (warp w drains TMEM
+//              lanes 32*(w%4)..+31, i.e. one output row per thread, and half
+//              of the tile's columns), scale, convert, stage in shared memory
+//              and TMA-store
 // TMEM holds two 128x256 int32 accumulators (512 columns), so the epilogue of
 // tile i overlaps the MMAs of tile i+1.
 //
@@ -49,11 +50,14 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
 constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTmemCols = 2 * BN;
 constexpr int GROUP_M = 16;
+// no alignment slack: the dynamic shared-memory window of a CTA without static
+// shared memory starts 1024-byte aligned (checked at run time)
 constexpr size_t kSmemBytes =
-    static_cast<size_t>(STAGES) * STAGE_BYTES + 4 * 3 * 32 * 64 + 2 * BN * 4 + 1024 + 256;
+    static_cast<size_t>(STAGES) * STAGE_BYTES + 8 * 2 * 32 * 64 + 2 * BN * 4 + 256;
 
 struct GemmArgs {
     void *out;
@@ -86,15 +90,15 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     atomicCAS(&g_gemm_fault, 0, 99);
 }
 
-// Epilogue staging.  Each epilogue warp owns three 2 KB buffers of 32 rows x 64
+// Epilogue staging.  Each epilogue warp owns two 2 KB buffers of 32 rows x 64
 // bytes (64-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ ((r>>1)&3),
 // the pattern the TMA store unswizzles).  A 32-column chunk of the warp's 32
 // rows (bf16; int32 uses 16-column chunks) is converted in registers, written
 // to one buffer and handed to a TMA bulk-tensor store, which also clips the
 // M/N tails; the next buffers are filled meanwhile.
 constexpr int kStageBytes = 32 * 64;
-constexpr int kStageBufs = 3;                           // per epilogue warp
-constexpr int kEpiSmem = 4 * kStageBufs * kStageBytes;  // 4 warps
+constexpr int kStageBufs = 2;                                  // per epilogue warp
+constexpr int kEpiSmem = kEpiWarps * kStageBufs * kStageBytes;
 
 __device__ __forceinline__ uint32_t stage_chunk_addr(uint32_t buf, int row, int c) {
     return buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4);
@@ -177,63 +181,53 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
     }
 }
 
-// Drain one accumulator tile.  TMEM loads are software-pipelined: the load of
-// chunk c+1 is in flight while chunk c is converted and staged.
+// Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
+// quarter) x half of the tile's columns, 32 columns at a time.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmOut, uint32_t taddr,
-                                              int m0, int n0, int quarter, int lane, float xs,
-                                              const float *s_ws, const float *s_b, uint32_t bufs,
-                                              int &bsel) {
+                                              int m0, int n0, int quarter, int half, int lane,
+                                              float xs, const float *s_ws, const float *s_b,
+                                              uint32_t bufs, int &bsel) {
     const int y = m0 + quarter * 32;
-    constexpr int NCH = (EPI == kEpiGegluBf16) ? 4 : BN / 32;  // 32-column chunks
-    const int nch = min(NCH, (a.N - n0 + 31) / 32);
+    constexpr int W = (EPI == kEpiGegluBf16) ? 64 : BN / 2;  // columns per warp
+    const int c0 = half * W;                                  // first column of this warp
     const f2 xs2 = mk2(xs, xs);
     const bool bias = a.bias != nullptr;
-    uint32_t ra[32], rb[32], ga[32], gb[32];
-    // chunk 0
-    tmem_ld32(taddr, ra);
-    if constexpr (EPI == kEpiGegluBf16) tmem_ld32(taddr + 128, ga);
-    tmem_wait_ld(ra);
-    if constexpr (EPI == kEpiGegluBf16) tmem_wait_ld(ga);
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-        if (c >= nch) break;
-        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-        uint32_t(&gcur)[32] = (c & 1) ? gb : ga;
-        uint32_t(&gnxt)[32] = (c & 1) ? ga : gb;
-        if (c + 1 < nch) {
-            tmem_ld32(taddr + (c + 1) * 32, nxt);
-            if constexpr (EPI == kEpiGegluBf16) tmem_ld32(taddr + 128 + (c + 1) * 32, gnxt);
-        }
+#pragma unroll 1
+    for (int c = c0; c < c0 + W; c += 32) {
+        if (n0 + c >= a.N) break;
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
         if constexpr (EPI == kEpiRawI32) {
+            tmem_wait_ld(r);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 stage_reserve(lane);
                 const uint32_t buf = bufs + bsel * kStageBytes;
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    st_shared_v4(stage_chunk_addr(buf, lane, q), cur[16 * h + 4 * q],
-                                 cur[16 * h + 4 * q + 1], cur[16 * h + 4 * q + 2],
-                                 cur[16 * h + 4 * q + 3]);
-                stage_flush(tmOut, buf, lane, n0 + c * 32 + 16 * h, y);
-                bsel = bsel + 1 == kStageBufs ? 0 : bsel + 1;
+                    st_shared_v4(stage_chunk_addr(buf, lane, q), r[16 * h + 4 * q],
+                                 r[16 * h + 4 * q + 1], r[16 * h + 4 * q + 2], r[16 * h + 4 * q + 3]);
+                stage_flush(tmOut, buf, lane, n0 + c + 16 * h, y);
+                bsel ^= 1;
             }
         } else {
             float v[32];
-            if constexpr (EPI == kEpiDequantBf16)
-                dequant32(cur, s_ws + c * 32, s_b + c * 32, xs2, bias, v);
-            else
-                geglu32(cur, gcur, s_ws + c * 32, s_ws + 128 + c * 32, xs2, v);
+            if constexpr (EPI == kEpiDequantBf16) {
+                tmem_wait_ld(r);
+                dequant32(r, s_ws + c, s_b + c, xs2, bias, v);
+            } else {
+                uint32_t rg[32];
+                tmem_ld32(taddr + 128 + c, rg);
+                tmem_wait_ld(r);
+                tmem_wait_ld(rg);
+                geglu32(r, rg, s_ws + c, s_ws + 128 + c, xs2, v);
+            }
             stage_reserve(lane);
             const uint32_t buf = bufs + bsel * kStageBytes;
             stage_bf16_32(buf, lane, v);
-            stage_flush(tmOut, buf, lane, n0 + c * 32, y);
-            bsel = bsel + 1 == kStageBufs ? 0 : bsel + 1;
-        }
-        if (c + 1 < nch) {
-            tmem_wait_ld(nxt);
-            if constexpr (EPI == kEpiGegluBf16) tmem_wait_ld(gnxt);
+            stage_flush(tmOut, buf, lane, n0 + c, y);
+            bsel ^= 1;
         }
     }
 }
@@ -242,9 +236,12 @@ template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw;
+    if (smem_u32(smem) & 1023u) {  // the 128-byte swizzle needs 1024-byte aligned tiles
+        if (threadIdx.x == 0) atomicCAS(&g_gemm_fault, 0, 98);
+        return;
+    }
     const uint32_t sA = smem_u32(smem);
     const uint32_t sB = sA + STAGES * A_BYTES;
     const uint32_t sEpi = sA + STAGES * STAGE_BYTES;  // 4 warps x 2 staging buffers
@@ -253,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(s_b + BN);
     const uint32_t bar0 = smem_u32(bars);
     const uint32_t final_bar = bar0 + 8 * (2 * STAGES + 4);
-    const uint32_t epi_bar = bar0 + 8 * (2 * STAGES + 5);  // the 128 epilogue threads
+    const uint32_t epi_bar = bar0 + 8 * (2 * STAGES + 5);  // the epilogue threads
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 6);
 #define FULL(s) (bar0 + 8u * (s))
 #define EMPTY(s) (bar0 + 8u * (STAGES + (s)))
@@ -270,10 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(TFULL(a), 1);
-            mbar_init(TEMPTY(a), 128);
+            mbar_init(TEMPTY(a), 32 * kEpiWarps);
         }
         mbar_init(final_bar, 1);
-        mbar_init(epi_bar, 128);
+        mbar_init(epi_bar, 32 * kEpiWarps);
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
@@ -369,42 +366,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
-        const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+        const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 2) >> 2;     // which half of the tile's columns
+        const int et = threadIdx.x - 64;      // 0..255 among the epilogue threads
         const uint32_t bufs = sEpi + (warp - 2) * kStageBufs * kStageBytes;
         int bsel = 0;
         int acc = 0;
         uint32_t aph = 0;
         uint32_t epi_phase = 0;
-        // a barrier of the 128 epilogue threads whose wait is bounded like every other
+        // a barrier of the epilogue threads whose wait is bounded like every other
         auto epi_sync = [&](int site) {
             mbar_arrive(epi_bar);
             const bool ok = mbar_wait(epi_bar, epi_phase & 1u, fault, site);
             ++epi_phase;
             return ok;
         };
+        // column et's scale and bias of a tile, read ahead of the tile (registers)
+        auto fetch = [&](int tile, float &w, float &b) {
+            int mb, nb;
+            tile_coords(tile, args.num_m, args.num_n, mb, nb);
+            const int n0 = nb * BN_OUT;
+            int n;
+            if constexpr (GEGLU) n = (et < 128) ? n0 + et : args.N + n0 + (et - 128);
+            else n = n0 + et;
+            const bool in = (n0 + (GEGLU ? (et & 127) : et)) < args.N;
+            w = (in && args.col_scale) ? __ldg(args.col_scale + n) : 1.f;
+            b = (in && args.bias) ? __ldg(args.bias + n) : 0.f;
+        };
+        float pre_w = 1.f, pre_b = 0.f;
+        if (static_cast<int>(blockIdx.x) < num_tiles) fetch(blockIdx.x, pre_w, pre_b);
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
             const int n0 = nb * BN_OUT;
-            // this tile's column scales and bias into shared memory
-            if (!epi_sync(5)) break;
-            for (int i = et; i < BN; i += 128) {
-                int n;
-                if constexpr (GEGLU) n = (i < 128) ? n0 + i : args.N + n0 + (i - 128);
-                else n = n0 + i;
-                const bool in = GEGLU ? (n0 + (i & 127)) < args.N : n < args.N;
-                s_ws[i] = (in && args.col_scale) ? __ldg(args.col_scale + n) : 1.f;
-                s_b[i] = (in && args.bias) ? __ldg(args.bias + n) : 0.f;
-            }
+            if (!epi_sync(5)) break;  // everyone is done with the previous tile's scales
+            s_ws[et] = pre_w;
+            s_b[et] = pre_b;
             if (!epi_sync(6)) break;
+            if (tile + static_cast<int>(gridDim.x) < num_tiles) fetch(tile + gridDim.x, pre_w, pre_b);
             if (!mbar_wait(TFULL(acc), aph, fault, 4)) break;
             tc_fence_after();
             const int row = mb * BM + quarter * 32 + lane;
             const float xs = (row < args.M && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
-            epilogue_tile<EPI>(args, &tmOut, taddr, mb * BM, n0, quarter, lane, xs, s_ws, s_b,
+            epilogue_tile<EPI>(args, &tmOut, taddr, mb * BM, n0, quarter, half, lane, xs, s_ws, s_b,
                                bufs, bsel);
             tc_fence_before();
             mbar_arrive(TEMPTY(acc));

@@ -223,9 +223,6 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         for (int k = 0; k < p.ns; ++k) issued += issue(k) ? 1 : 0;
 
     int k = 0;
-    int64_t pend_row0 = 0;
-    int pend_rows = 0;
-    uint32_t pend_stage = 0;
     for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
         const int st = k % p.ns;
         const int rows = batch_rows(b);
@@ -234,12 +231,6 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         // if any wait gave up
         const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
         if (!__syncthreads_and(ok)) break;
-        // the previous batch's output stage is complete: send it
-        if (threadIdx.x == 0 && pend_rows > 0) {
-            bulk_store(p.out + pend_row0 * p.out_row_bytes, pend_stage, pend_rows * p.out_row_bytes);
-            bulk_commit();
-        }
-        pend_rows = 0;
         const uint32_t stage = in_base + st * p.in_stage_bytes;
         unsigned int *amax_now = row_amax + 32 * (k % 3);
 
@@ -353,16 +344,12 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
                 }
             }
         }
-        // the stage is handed to the copy engine after the next barrier
         fence_async_smem();
-        pend_row0 = row0;
-        pend_rows = rows;
-        pend_stage = ostage;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && pend_rows > 0) {
-        bulk_store(p.out + pend_row0 * p.out_row_bytes, pend_stage, pend_rows * p.out_row_bytes);
-        bulk_commit();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store(p.out + row0 * p.out_row_bytes, ostage, rows * p.out_row_bytes);
+            bulk_commit();
+        }
     }
     if (threadIdx.x == 0) {
         // batches whose copies were issued but not consumed (after a fault)
