@@ -44,7 +44,6 @@ namespace {
 
 constexpr int kSlots = 16;             // half-warps per 256-thread CTA
 constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
-constexpr int kScratch = 512;          // behind each output stage: sink for invalid groups
 
 struct BulkParams {
     const uint8_t *in;
@@ -52,7 +51,7 @@ struct BulkParams {
     uint8_t *out;
     float *scale;            // mode 0: per-row output scale
     int64_t M, K;
-    int G, R, nbatch, ns;
+    int G, R, nbatch, ns, os;  // os: output stages (1 or 2)
     uint32_t in_row_bytes, out_row_bytes;
     uint32_t in_stage_bytes, out_stage_bytes;
 };
@@ -186,7 +185,7 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
     const uint32_t s0 = smem_u32(smem);
     const uint32_t in_base = s0;
     const uint32_t out_base = in_base + p.ns * p.in_stage_bytes;
-    const uint32_t tile_base = out_base + 2 * (p.out_stage_bytes + kScratch);
+    const uint32_t tile_base = out_base + p.os * p.out_stage_bytes;
     unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - s0) + kSlots * kTileBytes);
     uint64_t *fullb = reinterpret_cast<uint64_t *>(row_amax + 3 * 32);
     const uint32_t full0 = smem_u32(fullb);
@@ -289,11 +288,15 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         if constexpr (QUANT) {
             if (threadIdx.x < 32) row_amax[32 * ((k + 1) % 3) + threadIdx.x] = 0u;
         }
-        if (threadIdx.x == 0) bulk_wait_read<1>();  // out stage k&1 is free again
+        // the output stage this batch fills has been read by its last store
+        if (threadIdx.x == 0) {
+            if (p.os == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+        }
         __syncthreads();
         if (threadIdx.x == 0 && issue(k + p.ns)) ++issued;
 
-        const uint32_t ostage = out_base + (k & 1) * (p.out_stage_bytes + kScratch);
+        const uint32_t ostage = out_base + (k % p.os) * p.out_stage_bytes;
 #pragma unroll
         for (int j = 0; j < PPS; ++j) {
             const int f0 = 2 * (slot + kSlots * j), f1 = f0 + 1;
@@ -313,10 +316,11 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
                     if (g1 == 0 && l == 0) p.scale[row0 + r1] = s;
                 }
                 const f2 magic = mk2(12582912.0f, 12582912.0f);
-                // an invalid group of a pair writes into a scratch row of the
-                // stage (never stored), so the loop has no per-element branch
-                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + g0 * 256 + l : ostage + p.out_stage_bytes;
-                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + g1 * 256 + l : ostage + p.out_stage_bytes;
+                // an invalid group of a pair writes into the slot's transpose
+                // tile (free at this point, rewritten before its next read),
+                // so the loop has no per-element branch
+                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + g0 * 256 + l : tile + l;
+                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + g1 * 256 + l : tile + l;
 #pragma unroll
                 for (int w = 0; w < 16; ++w) {
                     // rint(v * (1/s)): |v/s| <= 127 (+ulps), so the low byte of
@@ -332,8 +336,8 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
                 }
             } else {
                 const f2 sixteenth = mk2(0.0625f, 0.0625f);
-                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2 : ostage + p.out_stage_bytes;
-                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2 : ostage + p.out_stage_bytes;
+                const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2 : tile + 2 * l;
+                const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2 : tile + 2 * l;
 #pragma unroll
                 for (int w = 0; w < 16; ++w) {
                     float x0, x1;
@@ -428,14 +432,24 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     const int64_t nb = (M + R - 1) / R;
     if (nb > 0x7FFFFFFF) return -1;
     p.nbatch = static_cast<int>(nb);
-    p.ns = 3;
-    auto total = [&](int ns) {
-        return static_cast<size_t>(ns) * p.in_stage_bytes + 2 * (p.out_stage_bytes + kScratch) +
+    // stage counts: the most CTAs per SM (228 KB of shared memory, 1 KB reserved
+    // per CTA), then the deepest input pipeline, then double-buffered output
+    auto total = [&](int ns, int os) {
+        return static_cast<size_t>(ns) * p.in_stage_bytes + static_cast<size_t>(os) * p.out_stage_bytes +
                kSlots * kTileBytes + 3 * 32 * 4 + 8 * ns;
     };
-    if (total(3) > 200 * 1024) p.ns = 2;
-    if (total(p.ns) > 200 * 1024) return -1;
-    const size_t smem = total(p.ns);
+    int best_ctas = 0;
+    p.ns = 0;
+    for (int ns : {3, 2}) {
+        for (int os : {2, 1}) {
+            const size_t t = total(ns, os);
+            if (t > 200 * 1024) continue;
+            const int ctas = static_cast<int>((228 * 1024) / (t + 1024));
+            if (ctas > best_ctas) { best_ctas = ctas; p.ns = ns; p.os = os; }
+        }
+    }
+    if (p.ns == 0) return -1;
+    const size_t smem = total(p.ns, p.os);
     if (mode == 0) {
         switch (act) {
             case 0: return launch_pps<0, 0>(s, p, pps, smem);
