@@ -43,6 +43,16 @@ __device__ int g_rot_fault = 0;
 namespace {
 
 constexpr int kSlots = 16;             // half-warps per 256-thread CTA
+// Input path: direct 16-byte loads into registers (default), or bulk copies
+// into shared-memory stages (the form this file started from, kept for A/B
+// builds with -DXPUINT8_ROTATE_STAGED).  The direct form needs no input
+// staging, so more CTAs fit per SM; the kernel is latency-bound, not
+// bandwidth-bound, at the staged form's occupancy.
+#ifdef XPUINT8_ROTATE_STAGED
+constexpr bool kDirect = false;
+#else
+constexpr bool kDirect = true;
+#endif
 constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
 
 struct BulkParams {
@@ -127,6 +137,38 @@ __device__ __forceinline__ void load16(const BulkParams &p, uint32_t stage, int 
     }
 }
 
+// the same 16 values loaded straight from global memory (row = absolute row)
+template <int MODE, int ACT>
+__device__ __forceinline__ void load16_global(const BulkParams &p, int64_t row, int g, int l,
+                                              float (&v)[16]) {
+    if constexpr (MODE == 3) {
+        const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(p.in + row * p.in_row_bytes + g * 256 + l * 16));
+        const float s = __ldg(p.row_scale + row);
+        const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                v[4 * j + t] = round_bf16(
+                    __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * t)) & 0xFF)), s));
+    } else {
+        const uint4 *base = reinterpret_cast<const uint4 *>(p.in + row * p.in_row_bytes + (g * 256 + l * 16) * 2);
+        const uint4 a0 = __ldcs(base), a1 = __ldcs(base + 1);
+        unpack16_bf16(a0, a1, v);
+        if constexpr (MODE == 0 && act_paired(ACT)) {
+            const uint4 *hb = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(base) + p.K * 2);
+            const uint4 b0 = __ldcs(hb), b1 = __ldcs(hb + 1);
+            float u[16];
+            unpack16_bf16(b0, b1, u);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], u[t]);
+        } else if constexpr (MODE == 0 && ACT != 0) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], 0.f);
+        }
+    }
+}
+
 // accumulation-chain radix-4 butterfly (unscaled) on fp32x2 lanes
 __device__ __forceinline__ void seq2(f2 &a0, f2 &a1, f2 &a2, f2 &a3) {
     const f2 p = add2(a0, a1), m = sub2(a0, a1);
@@ -178,8 +220,8 @@ __device__ __forceinline__ float halfwarp_max(float v) {
     return v;
 }
 
-template <int MODE, int ACT, int PPS>
-__global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
+template <int MODE, int ACT, int PPS, bool DIRECT>
+__global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(const BulkParams p) {
     constexpr bool QUANT = (MODE == 0);
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t s0 = smem_u32(smem);
@@ -218,18 +260,20 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
         return true;
     };
     int issued = 0;
-    if (threadIdx.x == 0)
+    if (!DIRECT && threadIdx.x == 0)
         for (int k = 0; k < p.ns; ++k) issued += issue(k) ? 1 : 0;
 
     int k = 0;
     for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
-        const int st = k % p.ns;
+        const int st = DIRECT ? 0 : k % p.ns;
         const int rows = batch_rows(b);
         const int64_t row0 = static_cast<int64_t>(b) * p.R;
         // every thread waits (acquiring the copy), and the CTA leaves together
         // if any wait gave up
-        const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
-        if (!__syncthreads_and(ok)) break;
+        if constexpr (!DIRECT) {
+            const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
+            if (!__syncthreads_and(ok)) break;
+        }
         const uint32_t stage = in_base + st * p.in_stage_bytes;
         unsigned int *amax_now = row_amax + 32 * (k % 3);
 
@@ -242,7 +286,9 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
             const bool v0 = f0 < groups && r0 < rows, v1 = f1 < groups && r1 < rows;
             float a[16], c[16];
             if (v0) {
-                if constexpr (MODE == 3) {
+                if constexpr (DIRECT) {
+                    load16_global<MODE, ACT>(p, row0 + r0, g0, l, a);
+                } else if constexpr (MODE == 3) {
                     BulkParams q = p;
                     q.row_scale = p.row_scale + row0;
                     load16<MODE, ACT>(q, stage, r0, g0, l, a);
@@ -254,7 +300,9 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
                 for (int t = 0; t < 16; ++t) a[t] = 0.f;
             }
             if (v1) {
-                if constexpr (MODE == 3) {
+                if constexpr (DIRECT) {
+                    load16_global<MODE, ACT>(p, row0 + r1, g1, l, c);
+                } else if constexpr (MODE == 3) {
                     BulkParams q = p;
                     q.row_scale = p.row_scale + row0;
                     load16<MODE, ACT>(q, stage, r1, g1, l, c);
@@ -294,7 +342,7 @@ __global__ void __launch_bounds__(256) rotate_bulk_kernel(const BulkParams p) {
             else bulk_wait_read<0>();
         }
         __syncthreads();
-        if (threadIdx.x == 0 && issue(k + p.ns)) ++issued;
+        if (!DIRECT && threadIdx.x == 0 && issue(k + p.ns)) ++issued;
 
         const uint32_t ostage = out_base + (k % p.os) * p.out_stage_bytes;
 #pragma unroll
@@ -390,9 +438,9 @@ int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
         return launch_status("rotate");
     };
     switch (pps) {
-        case 1: return pick(rotate_bulk_kernel<MODE, ACT, 1>);
-        case 2: return pick(rotate_bulk_kernel<MODE, ACT, 2>);
-        case 4: return pick(rotate_bulk_kernel<MODE, ACT, 4>);
+        case 1: return pick(rotate_bulk_kernel<MODE, ACT, 1, kDirect>);
+        case 2: return pick(rotate_bulk_kernel<MODE, ACT, 2, kDirect>);
+        case 4: return pick(rotate_bulk_kernel<MODE, ACT, 4, kDirect>);
         default: break;
     }
     set_error("unsupported group count per slot");
@@ -441,6 +489,14 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     int best_ctas = 0;
     p.ns = 0;
     for (int ns : {3, 2}) {
+        if (kDirect) {  // no input stages
+            for (int os : {2, 1}) {
+                const size_t t = total(0, os);
+                const int ctas = static_cast<int>((228 * 1024) / (t + 1024));
+                if (ctas > best_ctas) { best_ctas = ctas; p.ns = 1; p.os = os; }
+            }
+            break;
+        }
         for (int os : {2, 1}) {
             const size_t t = total(ns, os);
             if (t > 200 * 1024) continue;
@@ -449,7 +505,7 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
         }
     }
     if (p.ns == 0) return -1;
-    const size_t smem = total(p.ns, p.os);
+    const size_t smem = total(kDirect ? 0 : p.ns, p.os);
     if (mode == 0) {
         switch (act) {
             case 0: return launch_pps<0, 0>(s, p, pps, smem);
