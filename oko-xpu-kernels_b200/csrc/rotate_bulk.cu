@@ -226,7 +226,9 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t s0 = smem_u32(smem);
     const uint32_t in_base = s0;
-    const uint32_t out_base = in_base + p.ns * p.in_stage_bytes;
+    // the direct-load form has no input stages: its shared memory starts with
+    // the output stages (the host sizes it the same way)
+    const uint32_t out_base = in_base + (DIRECT ? 0u : p.ns * p.in_stage_bytes);
     const uint32_t tile_base = out_base + p.os * p.out_stage_bytes;
     unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - s0) + kSlots * kTileBytes);
     uint64_t *fullb = reinterpret_cast<uint64_t *>(row_amax + 3 * 32);
@@ -237,7 +239,7 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
     const uint32_t tile = tile_base + slot * kTileBytes;
     const int groups = p.R * p.G;
 
-    if (threadIdx.x == 0) {
+    if (!DIRECT && threadIdx.x == 0) {
         for (int s = 0; s < p.ns; ++s) mbar_init(full0 + 8 * s, 1);
         fence_mbar_init();
     }
@@ -489,11 +491,11 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     int best_ctas = 0;
     p.ns = 0;
     for (int ns : {3, 2}) {
-        if (kDirect) {  // no input stages
+        if (kDirect) {  // no input stages (p.ns = 0: the kernel's layout starts at the output stages)
             for (int os : {2, 1}) {
                 const size_t t = total(0, os);
                 const int ctas = static_cast<int>((228 * 1024) / (t + 1024));
-                if (ctas > best_ctas) { best_ctas = ctas; p.ns = 1; p.os = os; }
+                if (ctas > best_ctas) { best_ctas = ctas; p.ns = 0; p.os = os; }
             }
             break;
         }
@@ -504,8 +506,8 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
             if (ctas > best_ctas) { best_ctas = ctas; p.ns = ns; p.os = os; }
         }
     }
-    if (p.ns == 0) return -1;
-    const size_t smem = total(kDirect ? 0 : p.ns, p.os);
+    if (best_ctas == 0) return -1;
+    const size_t smem = total(p.ns, p.os);
     if (mode == 0) {
         switch (act) {
             case 0: return launch_pps<0, 0>(s, p, pps, smem);
