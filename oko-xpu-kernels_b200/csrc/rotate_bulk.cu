@@ -418,6 +418,248 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
     __syncthreads();
 }
 
+// The hot form of the family for K <= 8192: one pair of groups per slot, the
+// batch's R rows laid out over the 16 slots once per CTA (no per-batch index
+// arithmetic), global loads straight into registers one batch ahead (the
+// next batch's loads are in flight while this one is transformed), the row
+// scale computed once per pair when both groups share a row, output staged in
+// shared memory and written back by one bulk copy per batch.
+struct RawPair {
+    uint4 a0, a1, b0, b1;  // lane l's 32 bytes (bf16) or 16 bytes (int8) of each group
+    uint4 c0, c1, d0, d1;  // the second halves of a paired activation
+};
+
+template <int MODE, int ACT>
+__device__ __forceinline__ void load_raw(const BulkParams &p, int64_t row_a, int g_a, bool va,
+                                         int64_t row_b, int g_b, bool vb, int l, RawPair &r) {
+    if constexpr (MODE == 3) {
+        if (va) r.a0 = __ldcs(reinterpret_cast<const uint4 *>(p.in + row_a * p.in_row_bytes + g_a * 256 + l * 16));
+        if (vb) r.b0 = __ldcs(reinterpret_cast<const uint4 *>(p.in + row_b * p.in_row_bytes + g_b * 256 + l * 16));
+    } else {
+        if (va) {
+            const uint4 *s = reinterpret_cast<const uint4 *>(p.in + row_a * p.in_row_bytes + (g_a * 256 + l * 16) * 2);
+            r.a0 = __ldcs(s); r.a1 = __ldcs(s + 1);
+            if constexpr (MODE == 0 && act_paired(ACT)) {
+                const uint4 *h = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(s) + p.K * 2);
+                r.c0 = __ldcs(h); r.c1 = __ldcs(h + 1);
+            }
+        }
+        if (vb) {
+            const uint4 *s = reinterpret_cast<const uint4 *>(p.in + row_b * p.in_row_bytes + (g_b * 256 + l * 16) * 2);
+            r.b0 = __ldcs(s); r.b1 = __ldcs(s + 1);
+            if constexpr (MODE == 0 && act_paired(ACT)) {
+                const uint4 *h = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(s) + p.K * 2);
+                r.d0 = __ldcs(h); r.d1 = __ldcs(h + 1);
+            }
+        }
+    }
+}
+
+template <int MODE, int ACT>
+__device__ __forceinline__ void decode(const uint4 &x0, const uint4 &x1, const uint4 &y0,
+                                       const uint4 &y1, float s, float (&v)[16]) {
+    if constexpr (MODE == 3) {
+        const uint32_t w[4] = {x0.x, x0.y, x0.z, x0.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                v[4 * j + t] = round_bf16(
+                    __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * t)) & 0xFF)), s));
+    } else {
+        unpack16_bf16(x0, x1, v);
+        if constexpr (MODE == 0 && act_paired(ACT)) {
+            float u[16];
+            unpack16_bf16(y0, y1, u);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], u[t]);
+        } else if constexpr (MODE == 0 && ACT != 0) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], 0.f);
+        }
+    }
+}
+
+// s = max(rowmax / 127, 1e-30) (IEEE divide) and the quantizer's 1/s / 16
+__device__ __forceinline__ float row_inv16(float rowmax_x16, float &s) {
+    s = fmaxf(__fdiv_rn(__fmul_rn(rowmax_x16, 0.0625f), 127.0f), 1e-30f);
+    return __fmul_rn(__frcp_rn(s), 0.0625f);
+}
+
+#ifndef XPUINT8_DIRECT_MINB
+#define XPUINT8_DIRECT_MINB 4
+#endif
+// resident CTAs the register budget is fitted to (paired activations carry
+// twice the prefetched input)
+constexpr int direct_min_blocks(int mode, int act) {
+    return (mode == 0 && act_paired(act)) ? 2 : XPUINT8_DIRECT_MINB;
+}
+
+template <int MODE, int ACT>
+__global__ void __launch_bounds__(256, direct_min_blocks(MODE, ACT)) rotate_direct_kernel(const BulkParams p) {
+    constexpr bool QUANT = (MODE == 0);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t out_base = smem_u32(smem);
+    const uint32_t tile_base = out_base + p.os * p.out_stage_bytes;
+    unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - out_base) + kSlots * kTileBytes);
+
+    const int slot = threadIdx.x >> 4, l = threadIdx.x & 15;
+    const uint32_t tile = tile_base + slot * kTileBytes;
+    // this slot's pair of groups within a batch (the same for every batch)
+    const int f0 = 2 * slot, f1 = f0 + 1;
+    const int r0 = f0 / p.G, g0 = f0 - r0 * p.G;
+    const int r1 = f1 / p.G, g1 = f1 - r1 * p.G;
+    const bool in0 = f0 < p.R * p.G, in1 = f1 < p.R * p.G;
+    const bool same_row = r0 == r1;
+
+    if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
+    __syncthreads();
+
+    auto batch_rows = [&](int b) -> int {
+        const int64_t left = p.M - static_cast<int64_t>(b) * p.R;
+        return static_cast<int>(left < p.R ? left : p.R);
+    };
+    RawPair raw{};
+    if (static_cast<int>(blockIdx.x) < p.nbatch) {
+        const int rows = batch_rows(blockIdx.x);
+        const int64_t row0 = static_cast<int64_t>(blockIdx.x) * p.R;
+        load_raw<MODE, ACT>(p, row0 + r0, g0, in0 && r0 < rows, row0 + r1, g1, in1 && r1 < rows, l, raw);
+    }
+    int k = 0;
+    for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
+        const int rows = batch_rows(b);
+        const int64_t row0 = static_cast<int64_t>(b) * p.R;
+        const bool v0 = in0 && r0 < rows, v1 = in1 && r1 < rows;
+        unsigned int *amax_now = row_amax + 32 * (k % 3);
+
+        float a[16], c[16];
+        if (v0) {
+            decode<MODE, ACT>(raw.a0, raw.a1, raw.c0, raw.c1, MODE == 3 ? __ldg(p.row_scale + row0 + r0) : 0.f, a);
+        } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) a[t] = 0.f;
+        }
+        if (v1) {
+            decode<MODE, ACT>(raw.b0, raw.b1, raw.d0, raw.d1, MODE == 3 ? __ldg(p.row_scale + row0 + r1) : 0.f, c);
+        } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) c[t] = 0.f;
+        }
+        // the next batch's loads fly while this one is transformed
+        {
+            const int bn = b + gridDim.x;
+            if (bn < p.nbatch) {
+                const int rn = batch_rows(bn);
+                const int64_t rown = static_cast<int64_t>(bn) * p.R;
+                load_raw<MODE, ACT>(p, rown + r0, g0, in0 && r0 < rn, rown + r1, g1, in1 && r1 < rn, l, raw);
+            }
+        }
+        f2 vals[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) vals[t] = mk2(a[t], c[t]);
+        rotate_pair(vals, tile, l);
+        if constexpr (QUANT) {
+            float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                float x0, x1;
+                un2(vals[t], x0, x1);
+                m0 = fmaxf(m0, fabsf(x0));
+                m1 = fmaxf(m1, fabsf(x1));
+            }
+            if (same_row) {
+                m0 = halfwarp_max(fmaxf(m0, m1));
+                if (l == 0 && v0) atomicMax(amax_now + r0, __float_as_uint(m0));
+            } else {
+                m0 = halfwarp_max(m0);
+                m1 = halfwarp_max(m1);
+                if (l == 0) {
+                    if (v0) atomicMax(amax_now + r0, __float_as_uint(m0));
+                    if (v1) atomicMax(amax_now + r1, __float_as_uint(m1));
+                }
+            }
+            if (threadIdx.x < 32) row_amax[32 * ((k + 1) % 3) + threadIdx.x] = 0u;
+        }
+        // the output stage this batch fills has been read by its last store
+        if (threadIdx.x == 0) {
+            if (p.os == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+        }
+        __syncthreads();
+
+        const uint32_t ostage = out_base + (k % p.os) * p.out_stage_bytes;
+        if constexpr (QUANT) {
+            float s0 = 1.f, s1 = 1.f, inv0 = 0.f, inv1 = 0.f;
+            if (v0) inv0 = row_inv16(__uint_as_float(amax_now[r0]), s0);
+            if (same_row) {
+                inv1 = inv0;
+                s1 = s0;
+            } else if (v1) {
+                inv1 = row_inv16(__uint_as_float(amax_now[r1]), s1);
+            }
+            if (l == 0) {
+                if (v0 && g0 == 0) p.scale[row0 + r0] = s0;
+                if (v1 && g1 == 0) p.scale[row0 + r1] = s1;
+            }
+            const f2 magic = mk2(12582912.0f, 12582912.0f);
+            // an invalid group writes into the slot's transpose tile (free here,
+            // rewritten before its next read): no per-element branch
+            const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + g0 * 256 + l : tile + l;
+            const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + g1 * 256 + l : tile + l;
+#pragma unroll
+            for (int w = 0; w < 16; ++w) {
+                // rint(v * (1/s)) via the low byte of v/s + 1.5*2^23; the
+                // products are scalar __fmul_rn (a packed multiply feeding a
+                // packed add would be contracted into one FFMA2)
+                float x0, x1, q0, q1;
+                un2(vals[w], x0, x1);
+                un2(add2(mk2(__fmul_rn(x0, inv0), __fmul_rn(x1, inv1)), magic), q0, q1);
+                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o0 + 16 * w), "r"(__float_as_uint(q0)) : "memory");
+                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o1 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
+            }
+        } else {
+            const f2 sixteenth = mk2(0.0625f, 0.0625f);
+            const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2 : tile + 2 * l;
+            const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2 : tile + 2 * l;
+#pragma unroll
+            for (int w = 0; w < 16; ++w) {
+                float x0, x1;
+                un2(mul2(vals[w], sixteenth), x0, x1);
+                const uint32_t hb = cvt_bf16x2(x0, x1);
+                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o0 + 32 * w), "r"(hb & 0xFFFFu) : "memory");
+                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o1 + 32 * w), "r"(hb >> 16) : "memory");
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            bulk_store(p.out + row0 * p.out_row_bytes, ostage, rows * p.out_row_bytes);
+            bulk_commit();
+        }
+    }
+    if (threadIdx.x == 0) bulk_wait<0>();
+    __syncthreads();
+}
+
+template <int MODE, int ACT>
+int launch_direct(cudaStream_t s, const BulkParams &p, size_t smem) {
+    auto kern = rotate_direct_kernel<MODE, ACT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return launch_status("rotate (shared memory attribute)");
+    static size_t cached_smem = 0;
+    static int cached_per_sm = 0;
+    if (cached_smem != smem) {
+        int per = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess) per = 1;
+        cached_per_sm = std::max(1, per);
+        cached_smem = smem;
+    }
+    const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * cached_per_sm);
+    kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
+    return launch_status("rotate");
+}
+
 template <int MODE, int ACT>
 int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
     auto pick = [&](auto kern) -> int {
@@ -508,6 +750,22 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     }
     if (best_ctas == 0) return -1;
     const size_t smem = total(p.ns, p.os);
+    if (kDirect && pps == 1) {
+        if (mode == 0) {
+            switch (act) {
+                case 0: return launch_direct<0, 0>(s, p, smem);
+                case 1: return launch_direct<0, 1>(s, p, smem);
+                case 2: return launch_direct<0, 2>(s, p, smem);
+                case 3: return launch_direct<0, 3>(s, p, smem);
+                case 4: return launch_direct<0, 4>(s, p, smem);
+                case 5: return launch_direct<0, 5>(s, p, smem);
+                default: return -1;
+            }
+        }
+        if (mode == 2) return launch_direct<2, 0>(s, p, smem);
+        if (mode == 3) return launch_direct<3, 0>(s, p, smem);
+        return -1;
+    }
     if (mode == 0) {
         switch (act) {
             case 0: return launch_pps<0, 0>(s, p, pps, smem);
