@@ -214,9 +214,14 @@ __device__ __forceinline__ void rotate_pair(f2 (&P)[16], uint32_t tile, int l) {
     for (int j = 0; j < 4; ++j) bfly2(P[j], P[j + 4], P[j + 8], P[j + 12]);
 }
 
+// max over the 16 lanes of this thread's half-warp.  The mask names only that
+// half: the two slots of a warp may take different paths (a pair inside one
+// row reduces once, a pair across two rows twice), and a full-warp mask would
+// make them wait for each other's shuffles forever.
 __device__ __forceinline__ float halfwarp_max(float v) {
+    const unsigned mask = 0xFFFFu << (threadIdx.x & 16u);
 #pragma unroll
-    for (int m = 8; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    for (int m = 8; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(mask, v, m));
     return v;
 }
 
