@@ -165,6 +165,20 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
  * device synchronisation; reset != 0 clears it. */
 int xpuint8_fault_status(int32_t reset);
 
+/* xpuint8_linear_stream for callers that cannot allocate device memory (a
+ * plugin inside an application that owns the GPU's memory pool, a C caller
+ * without a device allocator, a path where cudaMalloc would synchronise).
+ * No counterpart in the reference.  Same arguments minus the scratch: the
+ * int8 activation and its row scales live in a fixed array inside the
+ * library (8 MiB + 64 KiB, held on every GPU that loads the library until
+ * exit), so M <= 16384 and M * K <= 8 MiB; larger calls return 2.  All calls
+ * on a device share that array: calls whose work overlaps on the GPU race.
+ * The first call on a device resolves the array's address (and may load the
+ * library's device code); make it before any stream capture. */
+int xpuint8_linear_noalloc_stream(const void *stream, const void *x, const int8_t *w8,
+                                  const float *w_scale, const float *bias, void *out, int64_t M,
+                                  int64_t N, int64_t K, int32_t activation);
+
 #ifdef __cplusplus
 }
 #endif
