@@ -1,0 +1,70 @@
+"""The sharded INT8 linear on two GPUs (NCCL), bit for bit against one GPU.
+
+Rows are independent, so the M-sharded result of each rank must equal the
+single-GPU result on those rows exactly; the N-sharded all-gather must rebuild
+the single-GPU output exactly.  Skipped when fewer than two GPUs are visible.
+"""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(dev):
+    import xpu_kernels
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(512, 1024, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(1024, 1024, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w8, ws = xpu_kernels.prepare_weight(w)
+    bias = torch.randn(1024, generator=g, device=dev) * 0.01
+    return x, w8, ws, bias
+
+
+def _worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    import xpu_kernels
+    from xpu_kernels.int8 import shard
+    x, w8, ws, bias = _problem(dev)
+    full = xpu_kernels.linear(x, w8, ws, bias)
+    a, b = shard.row_range(x.shape[0], world, rank)
+    ym = shard.linear_mshard(shard.split_rows(x, world, rank), w8, ws, bias)
+    w8l, wsl, bl = shard.shard_weight(w8, ws, world, rank, bias)
+    yn = shard.linear_nshard(x, w8l, wsl, bl, n_total=w8.shape[0])
+    torch.cuda.synchronize()
+    ok_m = torch.equal(ym.view(torch.int16), full[a:b].view(torch.int16))
+    ok_n = torch.equal(yn.view(torch.int16), full.view(torch.int16))
+    with open(os.path.join(outdir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{int(ok_m)} {int(ok_n)}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_linear_on_two_gpus(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                             join=False, start_method="spawn")
+    while not ctx.join(timeout=300):
+        pass
+    for r in range(world):
+        assert (tmp_path / f"r{r}.txt").read_text() == "1 1"
