@@ -16,27 +16,35 @@
 //           and gate rows [N+n, N+n+128) into one 256-wide B tile, and writes
 //           y = bf16(h * bf16(gelu_erf(g))) with h, g the bf16-rounded dequants
 //
-// Structure (one CTA per SM, persistent over output tiles, 320 threads):
-//   warp 0     TMA producer (one thread): A 128x128 and B 256x128 int8 tiles per
-//              k-block into a 4-stage shared-memory ring (128-byte swizzle)
-//   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
-//              tcgen05.mma.kind::i8 (128x256x32) per k-block, tcgen05.commit to
-//              free the ring slot and, per tile, to hand the accumulator over
-//   warps 2-9  epilogue: tcgen05.ld 32 columns at a time (warp w drains TMEM
-//              lanes 32*(w%4)..+31, i.e. one output row per thread, and half
-//              of the tile's columns), scale, convert, stage in shared memory
-//              and TMA-store
-// TMEM holds two 128x256 int32 accumulators (512 columns), so the epilogue of
-// tile i overlaps the MMAs of tile i+1.
+// Structure: persistent CTA pairs (clusters of 2 on neighbouring SMs, one CTA
+// per SM, 320 threads each) walk 256 x bn output tiles; the pair's MMAs are
+// tcgen05.mma.cta_group::2 (M = 256, N = bn <= 256, K = 32), which read each
+// operand half from the CTA that holds it.  Per k-block of 128 a CTA loads only
+// its 128 rows of A and bn/2 rows of B (32 KB, where a single-SM 128 x 256
+// tile needs 48 KB), which is what keeps the tensor pipe fed at short K.
+//   warp 0     TMA producer (one thread per CTA): 6-stage ring
+//              (128-byte swizzle); the bytes of both CTAs complete on the
+//              leader's FULL barrier
+//   warp 1     TMEM allocation in both CTAs; in the leader (rank 0) the MMA
+//              issuer: 4 MMAs per k-block, a commit to both CTAs' EMPTY
+//              barriers to free the slot, and per tile to both TFULL barriers
+//   warps 2-9  epilogue in both CTAs: tcgen05.ld 32 columns at a time (warp w
+//              drains TMEM lanes 32*(w%4)..+31, i.e. one output row per thread,
+//              and half of the tile's columns), scale, convert, stage in shared
+//              memory and TMA-store; each warp then arrives on the leader's
+//              TEMPTY barrier
+// TMEM holds two 128 x 256 int32 accumulators per CTA (512 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// No load here uses cluster multicast: every CTA fetches its own tiles, so the
-// kernel is safe to run with any operand in any GPU's memory.
+// No load here uses cluster multicast: every CTA fetches its own operand
+// halves, so the kernel is safe to run with any operand in any GPU's memory.
 //
 // Every mbarrier wait is bounded (common.cuh: mbar_wait); on a timeout the
 // kernel records the wait site in g_gemm_fault, drains its own TMA loads and
 // MMAs (again with a bound), frees its TMEM and returns.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -48,16 +56,12 @@ __device__ int g_gemm_fault = 0;
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
-constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each half the columns
-constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kTmemCols = 2 * BN;
+// A CTA pair computes a 256 x bn output tile (bn <= 256): each CTA holds 128
+// rows of A and bn/2 rows of B per k-block, and 128 accumulator rows.
+constexpr int BM = 128, BN = 256, BK = 128;
+constexpr int A_BYTES = BM * BK, B_BYTES = (BN / 2) * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int kTmemCols = 2 * BN;  // two accumulators of up to 256 columns
 constexpr int GROUP_M = 16;
-// no alignment slack: the dynamic shared-memory window of a CTA without static
-// shared memory starts 1024-byte aligned (checked at run time)
-constexpr size_t kSmemBytes =
-    static_cast<size_t>(STAGES) * STAGE_BYTES + 8 * 2 * 32 * 64 + 2 * BN * 4 + 256;
 
 struct GemmArgs {
     void *out;
@@ -67,6 +71,8 @@ struct GemmArgs {
     const float *bias;
     int M, N, K;
     int num_m, num_n, num_k;
+    int bn;  // output columns per tile (multiple of 32, 128..256); GEGLU: 128
+    // num_m counts 256-row pair tiles
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int &mb, int &nb) {
@@ -98,7 +104,24 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 // M/N tails; the next buffers are filled meanwhile.
 constexpr int kStageBytes = 32 * 64;
 constexpr int kStageBufs = 2;                                  // per epilogue warp
-constexpr int kEpiSmem = kEpiWarps * kStageBufs * kStageBytes;
+
+// Per-epilogue configuration.  The epilogue warps come in groups of four, one
+// per TMEM lane quarter (warp w reads lanes 32*(w%4)..+31), each group draining
+// its share of the tile's columns.  Two groups: a third or fourth group drains
+// the last tile sooner but costs a ring stage of shared memory and slows the
+// main loop more than it gains (measured at M=2048, N=10240, K=1280).  The ring
+// takes what shared memory the staging buffers leave (227 KB per CTA).
+template <int EPI>
+struct Cfg {
+    static constexpr int kEpiWarps = 8;
+    static constexpr int kGroups = kEpiWarps / 4;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+    static constexpr int kStages = 6;
+    static constexpr int kEpiSmem = kEpiWarps * kStageBufs * kStageBytes;
+    static constexpr size_t kSmemBytes =
+        static_cast<size_t>(kStages) * STAGE_BYTES + kEpiSmem + 2 * BN * 4 + 256;
+    static_assert(kSmemBytes <= 232448, "over the 227 KB shared-memory limit of a CTA");
+};
 
 __device__ __forceinline__ uint32_t stage_chunk_addr(uint32_t buf, int row, int c) {
     return buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4);
@@ -182,19 +205,17 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
 }
 
 // Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
-// quarter) x half of the tile's columns, 32 columns at a time.
+// quarter) x columns [c0, c1), 32 columns at a time.
 template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmOut, uint32_t taddr,
-                                              int m0, int n0, int quarter, int half, int lane,
+                                              int m0, int n0, int quarter, int c0, int c1, int lane,
                                               float xs, const float *s_ws, const float *s_b,
                                               uint32_t bufs, int &bsel) {
     const int y = m0 + quarter * 32;
-    constexpr int W = (EPI == kEpiGegluBf16) ? 64 : BN / 2;  // columns per warp
-    const int c0 = half * W;                                  // first column of this warp
     const f2 xs2 = mk2(xs, xs);
     const bool bias = a.bias != nullptr;
 #pragma unroll 1
-    for (int c = c0; c < c0 + W; c += 32) {
+    for (int c = c0; c < c1; c += 32) {
         if (n0 + c >= a.N) break;
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
@@ -233,19 +254,22 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmO
 }
 
 template <int EPI, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
+    constexpr int STAGES = Cfg<EPI>::kStages;
+    constexpr int kEpiWarps = Cfg<EPI>::kEpiWarps;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw;
     if (smem_u32(smem) & 1023u) {  // the 128-byte swizzle needs 1024-byte aligned tiles
+        // (the same layout in both CTAs of the pair: both leave here)
         if (threadIdx.x == 0) atomicCAS(&g_gemm_fault, 0, 98);
         return;
     }
     const uint32_t sA = smem_u32(smem);
     const uint32_t sB = sA + STAGES * A_BYTES;
-    const uint32_t sEpi = sA + STAGES * STAGE_BYTES;  // 4 warps x 2 staging buffers
-    float *s_ws = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + kEpiSmem);
+    const uint32_t sEpi = sA + STAGES * STAGE_BYTES;  // 2 staging buffers per epilogue warp
+    float *s_ws = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES + Cfg<EPI>::kEpiSmem);
     float *s_b = s_ws + BN;
     uint64_t *bars = reinterpret_cast<uint64_t *>(s_b + BN);
     const uint32_t bar0 = smem_u32(bars);
@@ -259,15 +283,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int *fault = &g_gemm_fault;
+    const uint32_t rank = cluster_rank();  // 0: the leader, which issues the pair's MMAs
+    const bool leader = rank == 0;
+    const int pair = static_cast<int>(cluster_index());
+    const int npairs = static_cast<int>(cluster_count());
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(FULL(s), 1);
-            mbar_init(EMPTY(s), 1);
+            mbar_init(FULL(s), 1);   // leader: its producer's expect_tx + both CTAs' bytes
+            mbar_init(EMPTY(s), 1);  // the leader's MMA commit
         }
         for (int a = 0; a < 2; ++a) {
-            mbar_init(TFULL(a), 1);
-            mbar_init(TEMPTY(a), 32 * kEpiWarps);
+            mbar_init(TFULL(a), 1);                // the leader's MMA commit
+            mbar_init(TEMPTY(a), 2 * kEpiWarps);   // leader: every epilogue warp of both CTAs
         }
         mbar_init(final_bar, 1);
         mbar_init(epi_bar, 32 * kEpiWarps);
@@ -276,9 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmB);
         prefetch_tmap(&tmOut);
     }
+    // both CTAs' barriers exist before either CTA arrives on the other's
+    cluster_sync();
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
     __syncthreads();
@@ -287,54 +317,62 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int num_tiles = args.num_m * args.num_n;
     constexpr bool GEGLU = (EPI == kEpiGegluBf16);
-    constexpr int BN_OUT = GEGLU ? 128 : BN;
+    const int BN_OUT = GEGLU ? 128 : args.bn;
+    const int B_ROWS = GEGLU ? BN : args.bn;  // MMA N: rows of B per pair tile
+    const int B_HALF = B_ROWS / 2;            // rows of B this CTA loads
 
     if (warp == 0) {
         if (lane == 0) {
-            // ------------------------------------------------------------ TMA producer
+            // ------------------------------------------------ TMA producer (both CTAs)
+            // Each CTA loads its own 128 rows of A and its half of B; the
+            // completion bytes of both count on the leader's FULL barrier, on
+            // which the leader's producer posted the pair's byte total.
             int stage = 0;
             uint32_t ph = 0;
             uint32_t issued = 0;  // k-blocks issued by this CTA
+            const uint32_t pair_tx = static_cast<uint32_t>(2 * (A_BYTES + B_HALF * BK));
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 int mb, nb;
                 tile_coords(tile, args.num_m, args.num_n, mb, nb);
+                const int arow = mb * (2 * BM) + static_cast<int>(rank) * BM;
                 for (int kb = 0; kb < args.num_k; ++kb) {
                     if (!mbar_wait(EMPTY(stage), ph ^ 1u, fault, 1)) { ok = false; break; }
-                    mbar_expect_tx(FULL(stage), STAGE_BYTES);
+                    if (leader) mbar_expect_tx(FULL(stage), pair_tx);
+                    const uint32_t fb = peer_smem(FULL(stage), 0);
                     const uint32_t dA = sA + stage * A_BYTES, dB = sB + stage * B_BYTES;
-                    if constexpr (A_MN) tma_load_2d(dA, &tmA, FULL(stage), mb * BM, kb * BK);
-                    else tma_load_2d(dA, &tmA, FULL(stage), kb * BK, mb * BM);
+                    if constexpr (A_MN) tma_load_2d_pair(dA, &tmA, fb, arow, kb * BK);
+                    else tma_load_2d_pair(dA, &tmA, fb, kb * BK, arow);
                     if constexpr (B_MN) {
-                        tma_load_2d(dB, &tmB, FULL(stage), nb * BN, kb * BK);
-                        tma_load_2d(dB + B_BYTES / 2, &tmB, FULL(stage), nb * BN + 128, kb * BK);
+                        tma_load_2d_pair(dB, &tmB, fb, nb * BN + static_cast<int>(rank) * 128, kb * BK);
                     } else if constexpr (GEGLU) {
-                        tma_load_2d(dB, &tmB, FULL(stage), kb * BK, nb * 128);
-                        tma_load_2d(dB + B_BYTES / 2, &tmB, FULL(stage), kb * BK, args.N + nb * 128);
+                        // leader: hidden rows [n, n+128); follower: gate rows [N+n, N+n+128)
+                        tma_load_2d_pair(dB, &tmB, fb, kb * BK, (leader ? 0 : args.N) + nb * 128);
                     } else {
-                        tma_load_2d(dB, &tmB, FULL(stage), kb * BK, nb * BN);
+                        tma_load_2d_pair(dB, &tmB, fb, kb * BK, nb * args.bn + static_cast<int>(rank) * B_HALF);
                     }
                     ++issued;
                     if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
             }
-            // our loads must have landed before the CTA can leave
-            // the last k-block issued into ring slot s was number i (i % STAGES == s)
+            // every load has landed once the MMAs that read it have completed:
+            // the last k-block issued into slot s (number i, i % STAGES == s)
+            // frees the slot in phase i / STAGES
             for (uint32_t s = 0; s < STAGES && s < issued; ++s) {
                 const uint32_t last = s + ((issued - 1 - s) / STAGES) * STAGES;
-                drain_wait(FULL(s), (last / STAGES) & 1u);
+                drain_wait(EMPTY(s), (last / STAGES) & 1u);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ------------------------------------------------------------ MMA issuer
-            constexpr uint32_t IDESC = umma_idesc_i8(BM, BN, A_MN, B_MN);
+        if (lane == 0 && leader) {
+            // ------------------------------------------------ MMA issuer (leader only)
+            const uint32_t idesc = umma_idesc_i8(2 * BM, B_ROWS, A_MN, B_MN);
             int stage = 0;
             uint32_t ph = 0;
             int acc = 0;
             uint32_t aph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 if (!mbar_wait(TEMPTY(acc), aph ^ 1u, fault, 2)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -350,26 +388,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                  : umma_sdesc_sw128(a0 + kk * 32, 16, 1024);
                         const uint64_t bd = B_MN ? umma_sdesc_sw128(b0 + kk * 4096, BK * 128, 1024)
                                                  : umma_sdesc_sw128(b0 + kk * 32, 16, 1024);
-                        umma_i8(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        umma_i8_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
-                    umma_commit(EMPTY(stage));
+                    // the slot is free in both CTAs once these MMAs have read it
+                    umma_commit_pair(EMPTY(stage));
+                    umma_commit_pair(peer_smem(EMPTY(stage), 1));
                     if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(TFULL(acc));
+                umma_commit_pair(TFULL(acc));
+                umma_commit_pair(peer_smem(TFULL(acc), 1));
                 acc ^= 1;
                 if (acc == 0) aph ^= 1u;
             }
             // every MMA this thread issued has completed once this barrier flips
-            umma_commit(final_bar);
+            umma_commit_pair(final_bar);
             drain_wait(final_bar, 0);
         }
     } else {
-        // ---------------------------------------------------------------- epilogue
+        // ---------------------------------------------------------- epilogue (both CTAs)
         const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
-        const int half = (warp - 2) >> 2;     // which half of the tile's columns
-        const int et = threadIdx.x - 64;      // 0..255 among the epilogue threads
+        const int group = (warp - 2) >> 2;    // which share of the tile's columns
+        // GEGLU: 64 output columns per group; otherwise BN / groups columns of
+        // the accumulator per group, clipped to the tile's bn
+        constexpr int kCols = GEGLU ? 64 : BN / Cfg<EPI>::kGroups;
+        const int col0 = kCols * group;
+        const int col1 = GEGLU ? col0 + kCols : min(col0 + kCols, args.bn);
+        const int et = threadIdx.x - 64;      // index among the epilogue threads; the
+                                              // first 256 stage the tile's column scales
         const uint32_t bufs = sEpi + (warp - 2) * kStageBufs * kStageBytes;
+        const uint32_t tempty_leader0 = peer_smem(TEMPTY(0), 0);
         int bsel = 0;
         int acc = 0;
         uint32_t aph = 0;
@@ -389,31 +437,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             int n;
             if constexpr (GEGLU) n = (et < 128) ? n0 + et : args.N + n0 + (et - 128);
             else n = n0 + et;
-            const bool in = (n0 + (GEGLU ? (et & 127) : et)) < args.N;
+            const bool in = GEGLU ? (n0 + (et & 127)) < args.N : (et < BN_OUT && n0 + et < args.N);
             w = (in && args.col_scale) ? __ldg(args.col_scale + n) : 1.f;
             b = (in && args.bias) ? __ldg(args.bias + n) : 0.f;
         };
         float pre_w = 1.f, pre_b = 0.f;
-        if (static_cast<int>(blockIdx.x) < num_tiles) fetch(blockIdx.x, pre_w, pre_b);
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const bool stager = et < 2 * BM;
+        if (stager && pair < num_tiles) fetch(pair, pre_w, pre_b);
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
             const int n0 = nb * BN_OUT;
+            const int m0 = mb * (2 * BM) + static_cast<int>(rank) * BM;
             if (!epi_sync(5)) break;  // everyone is done with the previous tile's scales
-            s_ws[et] = pre_w;
-            s_b[et] = pre_b;
+            if (stager) {
+                s_ws[et] = pre_w;
+                s_b[et] = pre_b;
+            }
             if (!epi_sync(6)) break;
-            if (tile + static_cast<int>(gridDim.x) < num_tiles) fetch(tile + gridDim.x, pre_w, pre_b);
+            if (stager && tile + npairs < num_tiles) fetch(tile + npairs, pre_w, pre_b);
+            const int row = m0 + quarter * 32 + lane;
+            const float xs = (row < args.M && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
             if (!mbar_wait(TFULL(acc), aph, fault, 4)) break;
             tc_fence_after();
-            const int row = mb * BM + quarter * 32 + lane;
-            const float xs = (row < args.M && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
-            epilogue_tile<EPI>(args, &tmOut, taddr, mb * BM, n0, quarter, half, lane, xs, s_ws, s_b,
-                               bufs, bsel);
+            epilogue_tile<EPI>(args, &tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
+                               s_b, bufs, bsel);
+            // hand the accumulator back to the leader's MMA issuer (one arrival per warp)
             tc_fence_before();
-            mbar_arrive(TEMPTY(acc));
+            __syncwarp();
+            if (lane == 0) {
+                if (leader) mbar_arrive(TEMPTY(acc));
+                else mbar_arrive_cluster(tempty_leader0 + 8u * acc);
+            }
             acc ^= 1;
             if (acc == 0) aph ^= 1u;
         }
@@ -425,10 +482,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #undef EMPTY
 #undef TFULL
 #undef TEMPTY
+    // neither CTA leaves while the other may still arrive on its barriers or
+    // (leader) read its shared memory and write its TMEM
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+    if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
 // -------------------------------------------------------------------------- host side
@@ -477,21 +536,64 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
     return true;
 }
 
+// CTA pairs that can be resident at once for this kernel (cached per device)
+template <int EPI, bool A_MN, bool B_MN>
+int resident_pairs(int dev) {
+    static int cached[32] = {0};
+    if (dev < 32 && cached[dev] > 0) return cached[dev];
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
+        return -1;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * num_sms());
+    cfg.blockDim = dim3(Cfg<EPI>::kThreads);
+    cfg.dynamicSmemBytes = Cfg<EPI>::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -1;
+    if (dev < 32) cached[dev] = n;
+    return n;
+}
+
 template <int EPI, bool A_MN, bool B_MN>
 int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
-                const GemmArgs &a, int grid) {
+                const GemmArgs &a, int pairs) {
     auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
-    static int configured_mask = 0;  // one bit per device ordinal (< 32)
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(Cfg<EPI>::kThreads);
+    cfg.dynamicSmemBytes = Cfg<EPI>::kSmemBytes;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, a) != cudaSuccess) return launch_status("gemm");
+    return launch_status("gemm");
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
+                 const CUtensorMap &mo, const GemmArgs &a, int64_t tiles) {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 32 || !(configured_mask & (1 << dev))) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kSmemBytes)) != cudaSuccess)
-            return launch_status("gemm (shared memory attribute)");
-        if (dev < 32) configured_mask |= (1 << dev);
+    const int resident = resident_pairs<EPI, A_MN, B_MN>(dev);
+    if (resident <= 0) {
+        set_error("no CTA pair of the GEMM fits on the device");
+        return 5;
     }
-    kern<<<grid, kThreads, kSmemBytes, s>>>(ma, mb, mo, a);
-    return launch_status("gemm");
+    const int pairs = static_cast<int>(tiles < resident ? tiles : resident);
+    return launch_inst<EPI, A_MN, B_MN>(s, ma, mb, mo, a, pairs);
 }
 
 }  // namespace
@@ -524,6 +626,33 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("scales and bias need 16-byte aligned bases");
         return 2;
     }
+    // Output columns per tile.  Tiles (256 rows x bn) are spread over the CTA
+    // pairs in waves (a persistent pair takes every P-th tile, P = pairs on
+    // the device), so the critical path is ceil(tiles / P) tiles; a narrower
+    // tile can finish sooner when it fills the last wave better (N = 10240 at
+    // M = 2048: 320 tiles of 256 columns take 5 waves of 74 pairs, 368 tiles
+    // of 224 columns also 5 waves of 7/8 the work).  Each tile also costs a
+    // fixed drain and hand-over, counted as 32 columns.  Only a K-major B is
+    // narrowed: an MN-major B tile is loaded as two 128-column boxes.
+    int bn = BN;
+    // XPUINT8_GEMM_BN=<128..256, multiple of 32> fixes the width (tests, tuning)
+    const char *force = std::getenv("XPUINT8_GEMM_BN");
+    const int forced = force ? std::atoi(force) : 0;
+    if (!geglu && !c.b_mn && forced >= 128 && forced <= BN && forced % 32 == 0) {
+        bn = forced;
+    } else if (!geglu && !c.b_mn) {
+        const int64_t sms = num_sms() / 2;  // CTA pairs
+        const int64_t num_m = (c.M + 2 * BM - 1) / (2 * BM);
+        int64_t best = -1;
+        for (int cand = BN; cand >= 128; cand -= 32) {
+            const int64_t tiles = num_m * ((c.N + cand - 1) / cand);
+            const int64_t cost = ((tiles + sms - 1) / sms) * (cand + 32);
+            if (best < 0 || cost < best) {
+                best = cost;
+                bn = cand;
+            }
+        }
+    }
     CUtensorMap ma, mb;
     // A: K-major [M rows, K bytes]; MN-major [K rows, M bytes]
     if (!c.a_mn) {
@@ -533,7 +662,8 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     }
     const int64_t b_rows = geglu ? 2 * c.N : c.N;
     if (!c.b_mn) {
-        if (!make_map(&mb, c.b, c.K, b_rows, c.ldb, BK, geglu ? 128 : BN)) return 2;
+        // each CTA of a pair loads half of the pair's B rows
+        if (!make_map(&mb, c.b, c.K, b_rows, c.ldb, BK, geglu ? 128 : bn / 2)) return 2;
     } else {
         if (!make_map(&mb, c.b, c.N, c.K, c.ldb, 128, BK)) return 2;
     }
@@ -552,28 +682,28 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     a.out = c.out; a.ldo = c.ldo;
     a.row_scale = c.row_scale; a.col_scale = c.col_scale; a.bias = c.bias;
     a.M = static_cast<int>(c.M); a.N = static_cast<int>(c.N); a.K = static_cast<int>(c.K);
-    a.num_m = static_cast<int>((c.M + BM - 1) / BM);
-    a.num_n = static_cast<int>((c.N + (geglu ? 128 : BN) - 1) / (geglu ? 128 : BN));
+    a.num_m = static_cast<int>((c.M + 2 * BM - 1) / (2 * BM));
+    a.bn = geglu ? 128 : bn;
+    a.num_n = static_cast<int>((c.N + a.bn - 1) / a.bn);
     a.num_k = static_cast<int>((c.K + BK - 1) / BK);
     const int64_t tiles = static_cast<int64_t>(a.num_m) * a.num_n;
     if (tiles > 0x7FFFFFFF) {
         set_error("too many output tiles");
         return 2;
     }
-    const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
     switch (c.epilogue) {
         case kEpiRawI32:
-            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiRawI32, false, false>(s, ma, mb, mo, a, grid);
-            if (!c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, false, true>(s, ma, mb, mo, a, grid);
-            if (c.a_mn && c.b_mn) return launch_inst<kEpiRawI32, true, true>(s, ma, mb, mo, a, grid);
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiRawI32, false, false>(s, ma, mb, mo, a, tiles);
+            if (!c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, false, true>(s, ma, mb, mo, a, tiles);
+            if (c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, true, true>(s, ma, mb, mo, a, tiles);
             break;
         case kEpiDequantBf16:
-            if (!c.a_mn && !c.b_mn) return launch_inst<kEpiDequantBf16, false, false>(s, ma, mb, mo, a, grid);
-            if (!c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, false, true>(s, ma, mb, mo, a, grid);
-            if (c.a_mn && c.b_mn) return launch_inst<kEpiDequantBf16, true, true>(s, ma, mb, mo, a, grid);
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantBf16, false, false>(s, ma, mb, mo, a, tiles);
+            if (!c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, false, true>(s, ma, mb, mo, a, tiles);
+            if (c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, true, true>(s, ma, mb, mo, a, tiles);
             break;
         case kEpiGegluBf16:
-            return launch_inst<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, grid);
+            return launch_sized<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, tiles);
         default:
             break;
     }

@@ -228,6 +228,32 @@ def test_int_mm_tn_is_bit_exact(m, n, k):
     assert np.array_equal(got, _exact(bits(a).T, bits(b)))
 
 
+@pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
+@pytest.mark.parametrize("m,n,k", [(300, 1040, 1280), (2048, 2080, 1280)])
+def test_every_tile_width_is_bit_exact(monkeypatch, bn, m, n, k):
+    """The GEMM picks its output-tile width (128..256 columns) from the shape;
+    XPUINT8_GEMM_BN pins it.  Every width gives the exact int32 product and the
+    same dequant bits, with ragged last tiles and several tiles per CTA."""
+    from xpu_kernels import int8
+    from xpu_kernels.int8 import _lib as L
+    monkeypatch.setenv("XPUINT8_GEMM_BN", str(bn))
+    lib = L.load()
+    a, b = rand_i8((m, k), 120 + bn), rand_i8((n, k), 121 + bn)
+    exact = _exact(bits(a), bits(b).T)
+    ad, bd = a.to(DEV), b.to(DEV)
+    assert np.array_equal(bits(int8.int_mm(ad, bd, 0)), exact)
+    g = torch.Generator().manual_seed(122)
+    xs, ws, bias = torch.rand(m, generator=g) * 1e-3, torch.rand(n, generator=g) * 1e-2, \
+        torch.randn(n, generator=g) * 0.1
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    xsd, wsd, bdd = (t.to(DEV) for t in (xs, ws, bias))
+    rc = lib.xpuint8_int_mm_dequant_stream(L._stream(out.device), L._ptr(ad), L._ptr(bd),
+                                           L._ptr(out), L._ptr(xsd), L._ptr(wsd), L._ptr(bdd),
+                                           m, n, k, 0, n)
+    assert rc == 0, lib.xpuint8_last_error()
+    assert np.array_equal(bits(out), O.dequant_epilogue(exact, bits(xs), bits(ws), bits(bias)))
+
+
 def test_int_mm_extreme_values_do_not_overflow():
     from xpu_kernels import int8
     k = 4096
