@@ -165,6 +165,14 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
  * device synchronisation; reset != 0 clears it. */
 int xpuint8_fault_status(int32_t reset);
 
+/* Self-check of the quantizers' scale arithmetic (blocking, default stream):
+ * the fast row scale s = max(amax/127, 1e-30) and 1/s against the IEEE
+ * divide / reciprocal on every non-negative float, and the packed
+ * product-then-add of the code computation against the scalar operations.
+ * Writes the mismatch counts (both 0 on a correct build).  No counterpart in
+ * the reference, whose quantizers call the divide per row. */
+int xpuint8_check_scale_math(int64_t *bad_scale, int64_t *bad_quant);
+
 /* xpuint8_linear_stream for callers that cannot allocate device memory (a
  * plugin inside an application that owns the GPU's memory pool, a C caller
  * without a device allocator, a path where cudaMalloc would synchronise).

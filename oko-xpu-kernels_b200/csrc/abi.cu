@@ -501,4 +501,12 @@ int xpuint8_fault_status(int32_t reset) {
     return g != 0 ? g : r;
 }
 
+int xpuint8_check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {
+    if (!bad_scale || !bad_quant) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    return check_scale_math(bad_scale, bad_quant);
+}
+
 }  // extern "C"

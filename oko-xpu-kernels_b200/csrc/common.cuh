@@ -364,6 +364,64 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
     return r;
 }
 
+// ---------------------------------------------------------------------------
+// The quantizers' per-row scale s = max(amax / 127, 1e-30) and its reciprocal,
+// both IEEE round-to-nearest, without the library divide / reciprocal calls
+// (each is a subroutine with a slow-path branch, and every warp of a
+// quantizer evaluates them once per row).
+//
+// div127_rn: division by the constant 127 with one FMA correction (Markstein,
+//   IBM J. Res. Dev. 34(1), 1990; Brisebarre, Muller and Raina, "Accelerating
+//   correctly rounded floating-point division when the divisor is known in
+//   advance", IEEE Trans. Computers 53(8), 2004):
+//   c = RN(1/127), q = RN(a c), r = a - 127 q (exact in one FMA), RN(q + r c).
+// rcp_rn: the hardware reciprocal estimate refined by two Newton-Raphson steps
+//   in FMA form, y' = RN(y + y RN(1 - s y)); the second is Markstein's
+//   correctly rounding iteration for an estimate within one ulp of 1/s.
+// row_scale_inv uses them for every finite amax and the library calls for
+// NaN and the few values above 3e38.  xpuint8_check_scale_math compares it with
+// the library-call form on every non-negative float, bit for bit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float div127_rn(float a) {
+    const float c = __uint_as_float(0x3C010204u);  // RN(1/127)
+    const float q = __fmul_rn(a, c);
+    const float r = __fmaf_rn(-q, 127.0f, a);
+    return __fmaf_rn(r, c, q);
+}
+__device__ __forceinline__ float rcp_rn(float s) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+    float e = __fmaf_rn(-s, y, 1.0f);
+    y = __fmaf_rn(y, e, y);
+    e = __fmaf_rn(-s, y, 1.0f);
+    return __fmaf_rn(y, e, y);
+}
+// s = max(amax / 127, 1e-30) and 1 / s
+__device__ __forceinline__ float row_scale_inv(float amax, float &s) {
+    if (amax <= 3.0e38f) {
+        s = fmaxf(div127_rn(amax), 1e-30f);
+        return rcp_rn(s);
+    }
+    s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    return __frcp_rn(s);
+}
+// the same with the library calls (the definition the fast form is checked against)
+__device__ __forceinline__ float row_scale_inv_lib(float amax, float &s) {
+    s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+    return __frcp_rn(s);
+}
+
+// rint(v * inv) for |v * inv| < 2^22, as fp32 bits whose low byte is the
+// two's-complement int8 code: the product rounded once (scalar mul.rn; ptxas
+// contracts a packed f32x2 multiply feeding a packed add into one FFMA2 even
+// without -fmad, which would round v*inv + 1.5*2^23 once instead of twice),
+// then the two sums of 1.5*2^23 as one packed add.
+__device__ __forceinline__ f2 quant_magic2(f2 v, float inv0, float inv1) {
+    float x0, x1;
+    un2(v, x0, x1);
+    return add2(mk2(__fmul_rn(x0, inv0), __fmul_rn(x1, inv1)), mk2(12582912.0f, 12582912.0f));
+}
+
 // UMMA shared-memory matrix descriptor, 128-byte swizzle (sm100 version 1).
 //   bits  0-13  start address >> 4
 //   bits 16-29  leading-dimension byte offset >> 4

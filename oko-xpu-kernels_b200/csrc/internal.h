@@ -25,6 +25,8 @@ int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const 
 int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
                        void *out, float *scale, int64_t M, int64_t K);
 int rot_fault_status(int reset);  // device fault word of the streaming rotation's waits
+// self-check of the quantizers' scale arithmetic (rotate_bulk.cu); counts mismatches
+int check_scale_math(int64_t *bad_scale, int64_t *bad_quant);
 
 // dequant epilogue (epilogue.cu)
 int launch_dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float *x_scale,

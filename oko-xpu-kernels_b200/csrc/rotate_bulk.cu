@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -426,34 +427,47 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
 // The hot form of the family for K <= 8192: one pair of groups per slot, the
 // batch's R rows laid out over the 16 slots once per CTA (no per-batch index
 // arithmetic), global loads straight into registers one batch ahead (the
-// next batch's loads are in flight while this one is transformed), the row
-// scale computed once per pair when both groups share a row, output staged in
-// shared memory and written back by one bulk copy per batch.
+// next batch's loads are in flight while this one is transformed).
+//
+// Per slot, shared memory holds the transpose tile (16 rows of 128 bytes at a
+// 144-byte pitch, so every access is a base register plus an immediate and a
+// half-warp's row writes and column reads are conflict-free), two output
+// buffers of one pair of groups, and 32 bytes of skew that put the two slots
+// of a warp on different banks.  A batch's groups are consecutive in the
+// dense output, so each slot writes its pair back with its own bulk copy from
+// its own buffer: the CTA synchronises once per batch, for the row abs-max.
 struct RawPair {
     uint4 a0, a1, b0, b1;  // lane l's 32 bytes (bf16) or 16 bytes (int8) of each group
     uint4 c0, c1, d0, d1;  // the second halves of a paired activation
 };
 
+constexpr int kPitch = 144;                 // transpose tile row pitch (128 data + 16 skew)
+constexpr int kTileP = 16 * kPitch;         // 2304 bytes
+__host__ __device__ constexpr int group_out_bytes(int mode) { return mode == 0 ? 256 : 512; }
+__host__ __device__ constexpr int slot_bytes(int mode) {
+    return kTileP + 4 * group_out_bytes(mode) + 32;
+}
+
 template <int MODE, int ACT>
-__device__ __forceinline__ void load_raw(const BulkParams &p, int64_t row_a, int g_a, bool va,
-                                         int64_t row_b, int g_b, bool vb, int l, RawPair &r) {
+__device__ __forceinline__ void load_raw(const uint8_t *pa, bool va, const uint8_t *pb, bool vb,
+                                         uint32_t half, RawPair &r) {
     if constexpr (MODE == 3) {
-        if (va) r.a0 = __ldcs(reinterpret_cast<const uint4 *>(p.in + row_a * p.in_row_bytes + g_a * 256 + l * 16));
-        if (vb) r.b0 = __ldcs(reinterpret_cast<const uint4 *>(p.in + row_b * p.in_row_bytes + g_b * 256 + l * 16));
+        if (va) r.a0 = __ldcs(reinterpret_cast<const uint4 *>(pa));
+        if (vb) r.b0 = __ldcs(reinterpret_cast<const uint4 *>(pb));
     } else {
         if (va) {
-            const uint4 *s = reinterpret_cast<const uint4 *>(p.in + row_a * p.in_row_bytes + (g_a * 256 + l * 16) * 2);
+            const uint4 *s = reinterpret_cast<const uint4 *>(pa);
             r.a0 = __ldcs(s); r.a1 = __ldcs(s + 1);
             if constexpr (MODE == 0 && act_paired(ACT)) {
-                const uint4 *h = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(s) + p.K * 2);
+                const uint4 *h = reinterpret_cast<const uint4 *>(pa + half);
                 r.c0 = __ldcs(h); r.c1 = __ldcs(h + 1);
             }
         }
         if (vb) {
-            const uint4 *s = reinterpret_cast<const uint4 *>(p.in + row_b * p.in_row_bytes + (g_b * 256 + l * 16) * 2);
+            const uint4 *s = reinterpret_cast<const uint4 *>(pb);
             r.b0 = __ldcs(s); r.b1 = __ldcs(s + 1);
             if constexpr (MODE == 0 && act_paired(ACT)) {
-                const uint4 *h = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(s) + p.K * 2);
+                const uint4 *h = reinterpret_cast<const uint4 *>(pb + half);
                 r.d0 = __ldcs(h); r.d1 = __ldcs(h + 1);
             }
         }
@@ -485,37 +499,77 @@ __device__ __forceinline__ void decode(const uint4 &x0, const uint4 &x1, const u
     }
 }
 
-// s = max(rowmax / 127, 1e-30) (IEEE divide) and the quantizer's 1/s / 16
-__device__ __forceinline__ float row_inv16(float rowmax_x16, float &s) {
-    s = fmaxf(__fdiv_rn(__fmul_rn(rowmax_x16, 0.0625f), 127.0f), 1e-30f);
-    return __fmul_rn(__frcp_rn(s), 0.0625f);
+// rotate_pair over the padded tile: P[q] = (A[16l+q], B[16l+q]) in,
+// P[w] = (A[16w+l], B[16w+l]) out (unscaled, x16)
+__device__ __forceinline__ void rotate_pair_padded(f2 (&P)[16], uint32_t tile, int l) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) seq2(P[4 * j], P[4 * j + 1], P[4 * j + 2], P[4 * j + 3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) seq2(P[j], P[j + 4], P[j + 8], P[j + 12]);
+    const uint32_t wrow = tile + l * kPitch;  // row l: P[0..15], 8 bytes each
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        float a0, b0, a1, b1;
+        un2(P[2 * c], a0, b0);
+        un2(P[2 * c + 1], a1, b1);
+        st_shared_v4(wrow + 16 * c, __float_as_uint(a0), __float_as_uint(b0), __float_as_uint(a1),
+                     __float_as_uint(b1));
+    }
+    __syncwarp();
+    const uint32_t rcol = tile + l * 8;       // column l of rows 0..15
+#pragma unroll
+    for (int w = 0; w < 16; ++w)
+        asm volatile("ld.shared.b64 %0, [%1];" : "=l"(P[w].v) : "r"(rcol + w * kPitch));
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly2(P[4 * j], P[4 * j + 1], P[4 * j + 2], P[4 * j + 3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly2(P[j], P[j + 4], P[j + 8], P[j + 12]);
 }
 
-#ifndef XPUINT8_DIRECT_MINB
-#define XPUINT8_DIRECT_MINB 4
+// Batches of loads in flight per thread.  Two (a ring of two register
+// buffers, the loop unrolled by two) for the rotations without quantization;
+// one for the quantizer, whose per-batch row-max barrier makes more resident
+// CTAs (8 of 64 registers a thread) worth more than a deeper prefetch
+// (measured at M = 65536, K = 4096: 4.0 TB/s against 3.7-3.9 TB/s).
+__host__ __device__ constexpr int direct_depth(int mode, int) {
+    return mode == 0 ? 1 : 2;
+}
+// resident 128-thread CTAs per SM the register budget is fitted to: 8 (64
+// registers a thread) at depth 1, XPUINT8_DIRECT_CTAS (96) at depth 2, 4 for
+// the paired activations
+#ifndef XPUINT8_DIRECT_CTAS
+#define XPUINT8_DIRECT_CTAS 5
 #endif
-// resident CTAs the register budget is fitted to (paired activations carry
-// twice the prefetched input)
-constexpr int direct_min_blocks(int mode, int act) {
-    return (mode == 0 && act_paired(act)) ? 2 : XPUINT8_DIRECT_MINB;
+constexpr int direct_min_ctas128(int mode, int act) {
+    return (mode == 0 && act_paired(act)) ? 4 : (direct_depth(mode, act) == 2 ? XPUINT8_DIRECT_CTAS : 8);
 }
 
-template <int MODE, int ACT>
-__global__ void __launch_bounds__(256, direct_min_blocks(MODE, ACT)) rotate_direct_kernel(const BulkParams p) {
+// SLOTS half-warps per CTA (8 or 16): the row abs-max barrier spans one CTA,
+// so the smaller CTA keeps it to the warps of one row at K <= 4096
+template <int MODE, int ACT, int SLOTS>
+__global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 / SLOTS)
+    rotate_direct_kernel(const BulkParams p) {
+    constexpr int DEPTH = direct_depth(MODE, ACT);
     constexpr bool QUANT = (MODE == 0);
+    constexpr int GOB = group_out_bytes(MODE);  // output bytes of one group
+    constexpr int IEB = (MODE == 3) ? 1 : 2;    // input bytes per element
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t out_base = smem_u32(smem);
-    const uint32_t tile_base = out_base + p.os * p.out_stage_bytes;
-    unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - out_base) + kSlots * kTileBytes);
-
     const int slot = threadIdx.x >> 4, l = threadIdx.x & 15;
-    const uint32_t tile = tile_base + slot * kTileBytes;
+    const uint32_t tile = smem_u32(smem) + slot * slot_bytes(MODE);
+    const uint32_t obuf = tile + kTileP;  // two buffers of one pair's output
+    unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + SLOTS * slot_bytes(MODE));
+
     // this slot's pair of groups within a batch (the same for every batch)
     const int f0 = 2 * slot, f1 = f0 + 1;
     const int r0 = f0 / p.G, g0 = f0 - r0 * p.G;
     const int r1 = f1 / p.G, g1 = f1 - r1 * p.G;
     const bool in0 = f0 < p.R * p.G, in1 = f1 < p.R * p.G;
     const bool same_row = r0 == r1;
+    // byte offsets inside a batch (a batch is at most 32 rows of at most 32 KB)
+    const uint32_t off0 = r0 * p.in_row_bytes + (g0 * 256 + l * 16) * IEB;
+    const uint32_t off1 = r1 * p.in_row_bytes + (g1 * 256 + l * 16) * IEB;
+    const uint32_t half = 2 * static_cast<uint32_t>(p.K);  // a paired activation's second half
 
     if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
     __syncthreads();
@@ -524,14 +578,17 @@ __global__ void __launch_bounds__(256, direct_min_blocks(MODE, ACT)) rotate_dire
         const int64_t left = p.M - static_cast<int64_t>(b) * p.R;
         return static_cast<int>(left < p.R ? left : p.R);
     };
-    RawPair raw{};
-    if (static_cast<int>(blockIdx.x) < p.nbatch) {
-        const int rows = batch_rows(blockIdx.x);
-        const int64_t row0 = static_cast<int64_t>(blockIdx.x) * p.R;
-        load_raw<MODE, ACT>(p, row0 + r0, g0, in0 && r0 < rows, row0 + r1, g1, in1 && r1 < rows, l, raw);
-    }
-    int k = 0;
-    for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
+    // load batch b (when it exists) into r
+    auto fetch = [&](int b, RawPair &r) {
+        if (b < p.nbatch) {
+            const int rows = batch_rows(b);
+            const uint8_t *src = p.in + static_cast<int64_t>(b) * p.R * p.in_row_bytes;
+            load_raw<MODE, ACT>(src + off0, in0 && r0 < rows, src + off1, in1 && r1 < rows, half, r);
+        }
+    };
+    // transform batch b (k-th of this CTA) from raw, whose registers then take
+    // the load of batch b + DEPTH * gridDim.x
+    auto batch = [&](int b, int k, RawPair &raw) {
         const int rows = batch_rows(b);
         const int64_t row0 = static_cast<int64_t>(b) * p.R;
         const bool v0 = in0 && r0 < rows, v1 = in1 && r1 < rows;
@@ -550,19 +607,14 @@ __global__ void __launch_bounds__(256, direct_min_blocks(MODE, ACT)) rotate_dire
 #pragma unroll
             for (int t = 0; t < 16; ++t) c[t] = 0.f;
         }
-        // the next batch's loads fly while this one is transformed
-        {
-            const int bn = b + gridDim.x;
-            if (bn < p.nbatch) {
-                const int rn = batch_rows(bn);
-                const int64_t rown = static_cast<int64_t>(bn) * p.R;
-                load_raw<MODE, ACT>(p, rown + r0, g0, in0 && r0 < rn, rown + r1, g1, in1 && r1 < rn, l, raw);
-            }
-        }
+        // the loads of DEPTH batches on fly while this one is transformed
+        fetch(b + DEPTH * static_cast<int>(gridDim.x), raw);
         f2 vals[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) vals[t] = mk2(a[t], c[t]);
-        rotate_pair(vals, tile, l);
+        rotate_pair_padded(vals, tile, l);
+
+        float inv0 = 0.f, inv1 = 0.f;
         if constexpr (QUANT) {
             float m0 = 0.f, m1 = 0.f;
 #pragma unroll
@@ -583,86 +635,99 @@ __global__ void __launch_bounds__(256, direct_min_blocks(MODE, ACT)) rotate_dire
                     if (v1) atomicMax(amax_now + r1, __float_as_uint(m1));
                 }
             }
+            // the buffer two batches on was last read before the previous barrier
             if (threadIdx.x < 32) row_amax[32 * ((k + 1) % 3) + threadIdx.x] = 0u;
-        }
-        // the output stage this batch fills has been read by its last store
-        if (threadIdx.x == 0) {
-            if (p.os == 2) bulk_wait_read<1>();
-            else bulk_wait_read<0>();
-        }
-        __syncthreads();
-
-        const uint32_t ostage = out_base + (k % p.os) * p.out_stage_bytes;
-        if constexpr (QUANT) {
-            float s0 = 1.f, s1 = 1.f, inv0 = 0.f, inv1 = 0.f;
-            if (v0) inv0 = row_inv16(__uint_as_float(amax_now[r0]), s0);
+            __syncthreads();  // every slot's contribution to this batch's row maxima
+            float s0 = 1.f, s1 = 1.f;
+            // the maxima are of x16 values: the scale is of max/16, the code v/16 * (1/s)
+            if (v0) inv0 = __fmul_rn(row_scale_inv(__fmul_rn(__uint_as_float(amax_now[r0]), 0.0625f), s0), 0.0625f);
             if (same_row) {
                 inv1 = inv0;
                 s1 = s0;
             } else if (v1) {
-                inv1 = row_inv16(__uint_as_float(amax_now[r1]), s1);
+                inv1 = __fmul_rn(row_scale_inv(__fmul_rn(__uint_as_float(amax_now[r1]), 0.0625f), s1), 0.0625f);
             }
             if (l == 0) {
                 if (v0 && g0 == 0) p.scale[row0 + r0] = s0;
                 if (v1 && g1 == 0) p.scale[row0 + r1] = s1;
             }
-            const f2 magic = mk2(12582912.0f, 12582912.0f);
-            // an invalid group writes into the slot's transpose tile (free here,
-            // rewritten before its next read): no per-element branch
-            const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + g0 * 256 + l : tile + l;
-            const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + g1 * 256 + l : tile + l;
+        }
+        // this slot's output buffer k&1: its bulk store of two batches ago has
+        // finished reading it
+        const uint32_t ob = obuf + (k & 1) * (2 * GOB);
+        if (l == 0) bulk_wait_read<1>();
+        __syncwarp();
+        if constexpr (QUANT) {
+            // rint(v * (1/s)), |v/s| <= 127 (+ulps); group A's codes at
+            // ob + 16w + l, group B's 256 bytes on
+            const uint32_t o = ob + l;
 #pragma unroll
             for (int w = 0; w < 16; ++w) {
-                // rint(v * (1/s)) via the low byte of v/s + 1.5*2^23; the
-                // products are scalar __fmul_rn (a packed multiply feeding a
-                // packed add would be contracted into one FFMA2)
-                float x0, x1, q0, q1;
-                un2(vals[w], x0, x1);
-                un2(add2(mk2(__fmul_rn(x0, inv0), __fmul_rn(x1, inv1)), magic), q0, q1);
-                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o0 + 16 * w), "r"(__float_as_uint(q0)) : "memory");
-                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o1 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
+                float q0, q1;
+                un2(quant_magic2(vals[w], inv0, inv1), q0, q1);
+                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o + 16 * w), "r"(__float_as_uint(q0)) : "memory");
+                asm volatile("st.shared.u8 [%0], %1;" ::"r"(o + 256 + 16 * w), "r"(__float_as_uint(q1)) : "memory");
             }
         } else {
             const f2 sixteenth = mk2(0.0625f, 0.0625f);
-            const uint32_t o0 = v0 ? ostage + r0 * p.out_row_bytes + (g0 * 256 + l) * 2 : tile + 2 * l;
-            const uint32_t o1 = v1 ? ostage + r1 * p.out_row_bytes + (g1 * 256 + l) * 2 : tile + 2 * l;
+            const uint32_t o = ob + 2 * l;
 #pragma unroll
             for (int w = 0; w < 16; ++w) {
                 float x0, x1;
                 un2(mul2(vals[w], sixteenth), x0, x1);
                 const uint32_t hb = cvt_bf16x2(x0, x1);
-                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o0 + 32 * w), "r"(hb & 0xFFFFu) : "memory");
-                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o1 + 32 * w), "r"(hb >> 16) : "memory");
+                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o + 32 * w), "r"(hb & 0xFFFFu) : "memory");
+                asm volatile("st.shared.u16 [%0], %1;" ::"r"(o + 512 + 32 * w), "r"(hb >> 16) : "memory");
             }
         }
         fence_async_smem();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            bulk_store(p.out + row0 * p.out_row_bytes, ostage, rows * p.out_row_bytes);
+        __syncwarp();
+        // the batch's groups are consecutive in the dense output: group f starts f * GOB bytes in
+        if (l == 0 && v0) {
+            bulk_store(p.out + row0 * p.out_row_bytes + f0 * GOB, ob, (v1 ? 2 : 1) * GOB);
             bulk_commit();
         }
+    };
+    RawPair ra{}, rb{};
+    fetch(blockIdx.x, ra);
+    if constexpr (DEPTH == 2) fetch(blockIdx.x + gridDim.x, rb);
+    int k = 0;
+    for (int b = blockIdx.x; b < p.nbatch;) {
+        batch(b, k, ra);
+        b += gridDim.x;
+        ++k;
+        if constexpr (DEPTH == 2) {
+            if (b >= p.nbatch) break;
+            batch(b, k, rb);
+            b += gridDim.x;
+            ++k;
+        }
     }
-    if (threadIdx.x == 0) bulk_wait<0>();
-    __syncthreads();
+    if (l == 0) bulk_wait<0>();
+    __syncwarp();
 }
 
-template <int MODE, int ACT>
-int launch_direct(cudaStream_t s, const BulkParams &p, size_t smem) {
-    auto kern = rotate_direct_kernel<MODE, ACT>;
+template <int MODE, int ACT, int SLOTS>
+int launch_direct(cudaStream_t s, const BulkParams &p) {
+    auto kern = rotate_direct_kernel<MODE, ACT, SLOTS>;
+    const size_t smem = static_cast<size_t>(SLOTS) * slot_bytes(MODE) + 3 * 32 * 4;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return launch_status("rotate (shared memory attribute)");
-    static size_t cached_smem = 0;
     static int cached_per_sm = 0;
-    if (cached_smem != smem) {
+    if (cached_per_sm == 0) {
         int per = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess) per = 1;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, SLOTS * 16, smem) != cudaSuccess)
+            per = 1;
         cached_per_sm = std::max(1, per);
-        cached_smem = smem;
     }
     const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * cached_per_sm);
-    kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
+    kern<<<static_cast<unsigned>(grid), SLOTS * 16, smem, s>>>(p);
     return launch_status("rotate");
+}
+template <int MODE, int ACT>
+int launch_direct(cudaStream_t s, const BulkParams &p, int slots) {
+    return slots == 8 ? launch_direct<MODE, ACT, 8>(s, p) : launch_direct<MODE, ACT, 16>(s, p);
 }
 
 template <int MODE, int ACT>
@@ -756,19 +821,30 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     if (best_ctas == 0) return -1;
     const size_t smem = total(p.ns, p.os);
     if (kDirect && pps == 1) {
+        // one batch per CTA-sized team of half-warps: 8 slots (128 threads)
+        // when a row has at most 16 groups, else 16
+        int slots = G <= 16 ? 8 : 16;
+        // XPUINT8_ROTATE_SLOTS=16 keeps 256-thread CTAs for every shape (tuning)
+        if (const char *f = std::getenv("XPUINT8_ROTATE_SLOTS")) {
+            if (std::atoi(f) == 16) slots = 16;
+        }
+        p.R = static_cast<int>(std::min<int64_t>(32, (2 * slots) / G));
+        const int64_t nbd = (M + p.R - 1) / p.R;
+        if (nbd > 0x7FFFFFFF) return -1;
+        p.nbatch = static_cast<int>(nbd);
         if (mode == 0) {
             switch (act) {
-                case 0: return launch_direct<0, 0>(s, p, smem);
-                case 1: return launch_direct<0, 1>(s, p, smem);
-                case 2: return launch_direct<0, 2>(s, p, smem);
-                case 3: return launch_direct<0, 3>(s, p, smem);
-                case 4: return launch_direct<0, 4>(s, p, smem);
-                case 5: return launch_direct<0, 5>(s, p, smem);
+                case 0: return launch_direct<0, 0>(s, p, slots);
+                case 1: return launch_direct<0, 1>(s, p, slots);
+                case 2: return launch_direct<0, 2>(s, p, slots);
+                case 3: return launch_direct<0, 3>(s, p, slots);
+                case 4: return launch_direct<0, 4>(s, p, slots);
+                case 5: return launch_direct<0, 5>(s, p, slots);
                 default: return -1;
             }
         }
-        if (mode == 2) return launch_direct<2, 0>(s, p, smem);
-        if (mode == 3) return launch_direct<3, 0>(s, p, smem);
+        if (mode == 2) return launch_direct<2, 0>(s, p, slots);
+        if (mode == 3) return launch_direct<3, 0>(s, p, slots);
         return -1;
     }
     if (mode == 0) {
@@ -785,6 +861,62 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     if (mode == 2) return launch_pps<2, 0>(s, p, pps, smem);
     if (mode == 3) return launch_pps<3, 0>(s, p, pps, smem);
     return -1;
+}
+
+// ---------------------------------------------------------------------------
+// Self-check of the quantizers' scale arithmetic (xpuint8_check_scale_math):
+// row_scale_inv against its library-call definition on every non-negative
+// float and +inf, and the code computation quant_magic2 against the scalar
+// IEEE operations on 2^31 pseudo-random (value, reciprocal) pairs whose
+// products fall in the code range, so that a contraction of the two roundings
+// into one would show.
+// ---------------------------------------------------------------------------
+__device__ unsigned long long g_scale_math_bad[2];
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16; x *= 0x7FEB352Du;
+    x ^= x >> 15; x *= 0x846CA68Bu;
+    x ^= x >> 16;
+    return x;
+}
+
+__global__ void check_scale_math_kernel() {
+    const uint64_t n = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    unsigned long long bad_scale = 0, bad_quant = 0;
+    for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u <= 0x7F800000ull;
+         u += n) {
+        const float a = __uint_as_float(static_cast<uint32_t>(u));
+        float s1, s2;
+        const float i1 = row_scale_inv(a, s1);
+        const float i2 = row_scale_inv_lib(a, s2);
+        bad_scale += (__float_as_uint(s1) != __float_as_uint(s2) || __float_as_uint(i1) != __float_as_uint(i2));
+        // v = +-1.m1 * 2^e1, inv = 1.m2 * 2^e2 with e1 + e2 in [-4, 5]: |v * inv| < 128
+        const uint32_t h1 = mix32(static_cast<uint32_t>(u) * 2u + 1u), h2 = mix32(h1 ^ 0x9E3779B9u);
+        const int e1 = static_cast<int>(h2 & 31u) - 16, e2 = static_cast<int>((h2 >> 5) % 10u) - 4 - e1;
+        const float v = __uint_as_float(((h1 & 1u) << 31) | static_cast<uint32_t>(127 + e1) << 23 | (h1 >> 9));
+        const float iv = __uint_as_float(static_cast<uint32_t>(127 + e2) << 23 | (h2 >> 9));
+        float p0, p1;
+        un2(quant_magic2(mk2(v, -v), iv, iv), p0, p1);
+        const float q = __fadd_rn(__fmul_rn(v, iv), 12582912.0f);
+        const float qn = __fadd_rn(__fmul_rn(-v, iv), 12582912.0f);
+        bad_quant += (__float_as_uint(p0) != __float_as_uint(q) || __float_as_uint(p1) != __float_as_uint(qn));
+    }
+    if (bad_scale) atomicAdd(&g_scale_math_bad[0], bad_scale);
+    if (bad_quant) atomicAdd(&g_scale_math_bad[1], bad_quant);
+}
+
+int check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {
+    const unsigned long long zero[2] = {0, 0};
+    if (cudaMemcpyToSymbol(g_scale_math_bad, zero, sizeof(zero)) != cudaSuccess)
+        return launch_status("scale-math check (reset)");
+    check_scale_math_kernel<<<num_sms() * 8, 256>>>();
+    if (const int rc = launch_status("scale-math check")) return rc;
+    unsigned long long got[2] = {0, 0};
+    if (cudaMemcpyFromSymbol(got, g_scale_math_bad, sizeof(got)) != cudaSuccess)
+        return launch_status("scale-math check (read)");
+    *bad_scale = static_cast<int64_t>(got[0]);
+    *bad_quant = static_cast<int64_t>(got[1]);
+    return 0;
 }
 
 int rot_fault_status(int reset) {

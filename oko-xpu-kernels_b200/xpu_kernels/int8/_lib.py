@@ -77,6 +77,7 @@ def _signatures():
         "xpuint8_quantize_row_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_colquant_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_fault_status": [i32],
+        "xpuint8_check_scale_math": [vp, vp],
         "xpuint8_linear_noalloc_stream": [vp] * 6 + [i64] * 3 + [i32],
     }
 

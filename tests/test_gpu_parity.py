@@ -118,6 +118,35 @@ def test_quantize_edge_rows():
     assert bits(s)[0] == np.float32(1e-30) and not bits(q)[0].any()
 
 
+def test_scale_math_matches_the_ieee_definition():
+    """The quantizers' row scale (s = max(amax/127, 1e-30), 1/s) without the
+    library divide equals the IEEE form on every non-negative float, and the
+    packed code arithmetic rounds the product and the sum separately."""
+    import ctypes
+    from xpu_kernels.int8 import _lib as L
+    bad_scale, bad_quant = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    rc = L.load().xpuint8_check_scale_math(ctypes.addressof(bad_scale), ctypes.addressof(bad_quant))
+    assert rc == 0, L.load().xpuint8_last_error()
+    assert (bad_scale.value, bad_quant.value) == (0, 0)
+
+
+def test_quantize_full_c5_every_code():
+    """Config C5's activation (x [65536, 4096], 0.5 % outlier channels x20):
+    every code and every row scale of the GPU rotate+quantize equals the
+    oracle's."""
+    from xpu_kernels import int8
+    m, k = 65536, 4096
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(m, k, generator=g, device=DEV)
+    x[:, torch.randperm(k, device=DEV, generator=g)[:20]] *= 20
+    x = x.to(torch.bfloat16)
+    q, s = int8.quantize(x)
+    for r in range(0, m, 8192):
+        qr, sr = O.convrot_quantize(bits(x[r:r + 8192]))
+        assert np.array_equal(bits(s[r:r + 8192]).view(np.uint32), sr.view(np.uint32)), r
+        assert np.array_equal(bits(q[r:r + 8192]), qr), r
+
+
 @pytest.mark.parametrize("act", ["gelu_tanh", "swiglu", "situ", "geglu_erf", "gelu_erf"])
 @pytest.mark.parametrize("m,k", [(5, 256), (64, 1280), (33, 4096)])
 def test_quantize_act(act, m, k):
