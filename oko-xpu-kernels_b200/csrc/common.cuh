@@ -139,6 +139,17 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start (prologue, barrier set-up, TMEM
+// allocation) while the kernel before it in the stream is still running.
+// pdl_wait() returns once every prerequisite grid has completed and its memory
+// operations are visible (a no-op for a kernel launched without the
+// attribute); pdl_trigger() lets the next such kernel begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // tcgen05: TMEM allocation (one full warp), MMA issue and commit (one thread),
 // TMEM -> register loads (one warp per 32-lane quarter).
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

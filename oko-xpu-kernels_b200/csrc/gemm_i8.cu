@@ -314,6 +314,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // everything above overlaps the previous kernel of the stream; operands,
+    // scales and the output are touched only after it has completed
+    pdl_wait();
 
     const int num_tiles = args.num_m * args.num_n;
     constexpr bool GEGLU = (EPI == kEpiGegluBf16);
@@ -355,6 +358,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
                     if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
             }
+            pdl_trigger();  // every load is issued: the next kernel may begin launching
             // every load has landed once the MMAs that read it have completed:
             // the last k-block issued into slot s (number i, i % STAGES == s)
             // frees the slot in phase i / STAGES
@@ -567,17 +571,21 @@ int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, co
                 const GemmArgs &a, int pairs) {
     auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // the prologue may overlap the previous kernel (the kernel waits for it
+    // before its first global access)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(Cfg<EPI>::kThreads);
     cfg.dynamicSmemBytes = Cfg<EPI>::kSmemBytes;
     cfg.stream = s;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, a) != cudaSuccess) return launch_status("gemm");
     return launch_status("gemm");
 }

@@ -573,6 +573,11 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
 
     if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
     __syncthreads();
+    // launched with programmatic serialization: the input and the outputs are
+    // touched only once the previous kernel of the stream has completed; the
+    // next kernel (the GEMM that reads the codes) may start its prologue now
+    pdl_wait();
+    pdl_trigger();
 
     auto batch_rows = [&](int b) -> int {
         const int64_t left = p.M - static_cast<int64_t>(b) * p.R;
@@ -722,7 +727,17 @@ int launch_direct(cudaStream_t s, const BulkParams &p) {
         cached_per_sm = std::max(1, per);
     }
     const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * cached_per_sm);
-    kern<<<static_cast<unsigned>(grid), SLOTS * 16, smem, s>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(SLOTS * 16);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return launch_status("rotate");
     return launch_status("rotate");
 }
 template <int MODE, int ACT>
