@@ -422,15 +422,26 @@ __device__ __forceinline__ float row_scale_inv_lib(float amax, float &s) {
     return __frcp_rn(s);
 }
 
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+    return r;
+}
 // rint(v * inv) for |v * inv| < 2^22, as fp32 bits whose low byte is the
-// two's-complement int8 code: the product rounded once (scalar mul.rn; ptxas
-// contracts a packed f32x2 multiply feeding a packed add into one FFMA2 even
-// without -fmad, which would round v*inv + 1.5*2^23 once instead of twice),
-// then the two sums of 1.5*2^23 as one packed add.
+// two's-complement int8 code: p = RN(v * inv), then RN(p * 1 + 1.5*2^23).
+// The sum is written as an FMA with an exact unit product because ptxas
+// contracts a packed multiply feeding a packed add into one FFMA2 even
+// without -fmad (rounding v*inv + 1.5*2^23 once instead of twice); an FMA's
+// multiplicand cannot absorb another multiply.  xpuint8_check_scale_math
+// checks the result against the scalar operations.
 __device__ __forceinline__ f2 quant_magic2(f2 v, float inv0, float inv1) {
-    float x0, x1;
-    un2(v, x0, x1);
-    return add2(mk2(__fmul_rn(x0, inv0), __fmul_rn(x1, inv1)), mk2(12582912.0f, 12582912.0f));
+    return fma2(mul2(v, mk2(inv0, inv1)), mk2(1.0f, 1.0f), mk2(12582912.0f, 12582912.0f));
+}
+// max(m, |a|, |b|) in one three-input maximum
+__device__ __forceinline__ float max3_abs(float m, float a, float b) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+    return r;
 }
 
 // UMMA shared-memory matrix descriptor, 128-byte swizzle (sm100 version 1).

@@ -621,13 +621,16 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
 
         float inv0 = 0.f, inv1 = 0.f;
         if constexpr (QUANT) {
+            // per-group maxima of |v| over the slot's half-warp, three-input
+            // maxima over pairs of values
             float m0 = 0.f, m1 = 0.f;
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-                float x0, x1;
-                un2(vals[t], x0, x1);
-                m0 = fmaxf(m0, fabsf(x0));
-                m1 = fmaxf(m1, fabsf(x1));
+            for (int t = 0; t < 16; t += 2) {
+                float a0, b0, a1, b1;
+                un2(vals[t], a0, b0);
+                un2(vals[t + 1], a1, b1);
+                m0 = max3_abs(m0, a0, a1);
+                m1 = max3_abs(m1, b0, b1);
             }
             if (same_row) {
                 m0 = halfwarp_max(fmaxf(m0, m1));
