@@ -416,6 +416,13 @@ __device__ __forceinline__ float row_scale_inv(float amax, float &s) {
     s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
     return __frcp_rn(s);
 }
+// RN(x / s) given y = RN(1 / s): Markstein's correction of the product with
+// the reciprocal, q0 = RN(x y), r = x - s q0 (exact in one FMA), RN(q0 + r y)
+__device__ __forceinline__ float div_by_rcp(float x, float s, float y) {
+    const float q0 = __fmul_rn(x, y);
+    const float r = __fmaf_rn(-q0, s, x);
+    return __fmaf_rn(r, y, q0);
+}
 // the same with the library calls (the definition the fast form is checked against)
 __device__ __forceinline__ float row_scale_inv_lib(float amax, float &s) {
     s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <string>
 
 #include "common.cuh"
 #include "internal.h"
@@ -883,13 +884,18 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
 
 // ---------------------------------------------------------------------------
 // Self-check of the quantizers' scale arithmetic (xpuint8_check_scale_math):
-// row_scale_inv against its library-call definition on every non-negative
-// float and +inf, and the code computation quant_magic2 against the scalar
-// IEEE operations on 2^31 pseudo-random (value, reciprocal) pairs whose
-// products fall in the code range, so that a contraction of the two roundings
-// into one would show.
+// [0] row_scale_inv against its library-call definition on every
+//     non-negative float and +inf;
+// [1] the code computation quant_magic2 against the scalar IEEE operations on
+//     2^31 pseudo-random (value, reciprocal) pairs whose products fall in the
+//     code range, so that a contraction of the two roundings into one shows;
+// [2] the row quantizer's code rint(div_by_rcp(x, s, 1/s)) against
+//     rint(x / s) with the IEEE division, for every bf16 x and every bf16 row
+//     maximum amax >= |x| (s the row scale of amax): all the pairs that
+//     quantizer can meet;
+// [3] the same for the column quantizer on 2^31 pseudo-random fp32 pairs.
 // ---------------------------------------------------------------------------
-__device__ unsigned long long g_scale_math_bad[2];
+__device__ unsigned long long g_scale_math_bad[4];
 
 __device__ __forceinline__ uint32_t mix32(uint32_t x) {
     x ^= x >> 16; x *= 0x7FEB352Du;
@@ -898,9 +904,14 @@ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
     return x;
 }
 
+// the int8 code of a quotient: clamp(rint(q), +-127)
+__device__ __forceinline__ int code_of(float q) {
+    return static_cast<int>(fmaxf(-127.f, fminf(127.f, rintf(q))));
+}
+
 __global__ void check_scale_math_kernel() {
     const uint64_t n = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    unsigned long long bad_scale = 0, bad_quant = 0;
+    unsigned long long bad_scale = 0, bad_quant = 0, bad_rowdiv = 0, bad_coldiv = 0;
     for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u <= 0x7F800000ull;
          u += n) {
         const float a = __uint_as_float(static_cast<uint32_t>(u));
@@ -918,22 +929,47 @@ __global__ void check_scale_math_kernel() {
         const float q = __fadd_rn(__fmul_rn(v, iv), 12582912.0f);
         const float qn = __fadd_rn(__fmul_rn(-v, iv), 12582912.0f);
         bad_quant += (__float_as_uint(p0) != __float_as_uint(q) || __float_as_uint(p1) != __float_as_uint(qn));
+        // [2] bf16 x over bf16 amax >= |x|
+        const uint32_t ab = static_cast<uint32_t>(u >> 16), xb = static_cast<uint32_t>(u & 0xFFFFu);
+        const float am = bf16_bits_to_f32(ab), xv = bf16_bits_to_f32(xb);
+        if (ab < 0x7F80u && (xb & 0x7FFFu) <= ab) {
+            float s;
+            const float y = row_scale_inv(am, s);
+            bad_rowdiv += code_of(div_by_rcp(xv, s, y)) != code_of(__fdiv_rn(xv, s));
+        }
+        // [3] fp32 g over a column maximum >= |g|
+        {
+            const uint32_t h3 = mix32(h2 + 0x632BE5ABu), h4 = mix32(h3 ^ 0x85EBCA6Bu);
+            const float g = __uint_as_float((h3 & 0x80000000u) | (static_cast<uint32_t>(64 + (h3 >> 1) % 128u) << 23) |
+                                            (h4 >> 9));
+            const float cm = __fmul_rn(fabsf(g), __uint_as_float(0x3F800000u | (mix32(h4) >> 9)));
+            float s;
+            const float y = row_scale_inv(cm, s);
+            bad_coldiv += code_of(div_by_rcp(g, s, y)) != code_of(__fdiv_rn(g, s));
+        }
     }
     if (bad_scale) atomicAdd(&g_scale_math_bad[0], bad_scale);
     if (bad_quant) atomicAdd(&g_scale_math_bad[1], bad_quant);
+    if (bad_rowdiv) atomicAdd(&g_scale_math_bad[2], bad_rowdiv);
+    if (bad_coldiv) atomicAdd(&g_scale_math_bad[3], bad_coldiv);
 }
 
 int check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {
-    const unsigned long long zero[2] = {0, 0};
+    const unsigned long long zero[4] = {0, 0, 0, 0};
     if (cudaMemcpyToSymbol(g_scale_math_bad, zero, sizeof(zero)) != cudaSuccess)
         return launch_status("scale-math check (reset)");
     check_scale_math_kernel<<<num_sms() * 8, 256>>>();
     if (const int rc = launch_status("scale-math check")) return rc;
-    unsigned long long got[2] = {0, 0};
+    unsigned long long got[4] = {0, 0, 0, 0};
     if (cudaMemcpyFromSymbol(got, g_scale_math_bad, sizeof(got)) != cudaSuccess)
         return launch_status("scale-math check (read)");
+    // the scale counts; the code and division counts together
     *bad_scale = static_cast<int64_t>(got[0]);
-    *bad_quant = static_cast<int64_t>(got[1]);
+    *bad_quant = static_cast<int64_t>(got[1] + got[2] + got[3]);
+    if (got[1] || got[2] || got[3])
+        set_error("scale-math check: code " + std::to_string(got[1]) + ", row division " +
+                  std::to_string(got[2]) + ", column division " + std::to_string(got[3]) +
+                  " mismatches");
     return 0;
 }
 

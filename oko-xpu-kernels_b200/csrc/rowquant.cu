@@ -6,20 +6,34 @@
 //   (python/xpu_kernels/int8/ops.py:320-330): scale = max(amax / 127, 1e-30),
 //   q = clamp(rint(x / scale), +-127), both true IEEE divisions; the column
 //   scale product follows ops.py:365 (bf16 * bf16 -> bf16).
-//   One CTA per row; the row is read twice (the second read hits L2).
+//   For K <= 8192 a 128-thread CTA holds a row in registers (one read of the
+//   input, the next row's loads in flight while this one is quantized, one
+//   barrier per row); longer rows are read twice (the second read hits L2).
 //
 // colquant: the operand of the int8 weight gradient.  g[m,n] = dy[m,n]*xs[m]
 //   (fp32), per-column tg[n] = max(amax_m |g| / 127, 1e-30),
 //   gq[m,n] = clamp(rint(g / tg[n]), +-127).  Three launches: column abs-max
 //   (atomicMax on the bit pattern of a non-negative float), scale, quantize.
+//
+// Division.  Every x / s is RN(x / s) computed as Markstein's correction of
+// the product with the correctly rounded reciprocal y = RN(1 / s) (Markstein,
+// IBM J. Res. Dev. 34(1), 1990): q0 = RN(x y), r = x - s q0 (exact in one
+// FMA), RN(q0 + r y).  For the row quantizer the operands are bf16 values and
+// RN(bf16 / 127) divisors, 2^31 pairs in all, and xpuint8_check_scale_math
+// compares every one of them with the IEEE division; the column quantizer's
+// quotients are checked against it on pseudo-random pairs.
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace xpuint8 {
 namespace {
 
-__device__ __forceinline__ int8_t q_div(float x, float s) {
-    const float r = rintf(__fdiv_rn(x, s));
+// clamp(rint(x / s), +-127) given y = RN(1 / s)
+__device__ __forceinline__ int8_t q_div(float x, float s, float y) {
+    const float r = rintf(div_by_rcp(x, s, y));
     return static_cast<int8_t>(fmaxf(-127.f, fminf(127.f, r)));
 }
 
@@ -69,7 +83,8 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
     __syncthreads();
     float rm = 0.f;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) rm = fmaxf(rm, red[w]);
-    const float s = fmaxf(__fdiv_rn(rm, 127.0f), 1e-30f);
+    float s;
+    const float y = row_scale_inv(rm, s);
     if (threadIdx.x == 0) scale[row] = s;
     for (int64_t k = threadIdx.x * 8; k < kv; k += blockDim.x * 8) {
         float v[8];
@@ -77,7 +92,7 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
         uint2 o;
         uint32_t b[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) b[t] = static_cast<uint8_t>(q_div(v[t], s));
+        for (int t = 0; t < 8; ++t) b[t] = static_cast<uint8_t>(q_div(v[t], s, y));
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
         o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
         *reinterpret_cast<uint2 *>(qr + k) = o;
@@ -85,7 +100,91 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
     for (int64_t k = kv + threadIdx.x; k < K; k += blockDim.x) {
         float v = bf16_bits_to_f32(xr[k]);
         if constexpr (COLSCALE) v = round_bf16(__fmul_rn(v, round_bf16(cs[k])));
-        qr[k] = q_div(v, s);
+        qr[k] = q_div(v, s, y);
+    }
+}
+
+// Register-resident form for K <= 8192: a 128-thread CTA per row at a time
+// (persistent over rows); thread t owns the 8-element chunks t, t + 128, ...
+// (CH of them).  The next row's loads are issued before this row is
+// quantized; one barrier per row (double-buffered warp maxima).
+template <bool COLSCALE, int CH>
+__global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *__restrict__ x,
+                                                               const float *__restrict__ cs,
+                                                               int8_t *__restrict__ q,
+                                                               float *__restrict__ scale,
+                                                               int64_t M, int64_t K) {
+    __shared__ float red[2][4];
+    const int t = threadIdx.x;
+    const int nch = static_cast<int>(K >> 3);
+    uint32_t csb[COLSCALE ? CH * 4 : 1];  // bf16(col_scale) of this thread's columns, in pairs
+    if constexpr (COLSCALE) {
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int ch = t + 128 * c;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                csb[4 * c + j] = ch < nch ? pack_bf16x2(__ldg(cs + 8 * ch + 2 * j), __ldg(cs + 8 * ch + 2 * j + 1)) : 0u;
+        }
+    }
+    auto load = [&](int64_t row, uint4 (&raw)[CH]) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + row * K);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int ch = t + 128 * c;
+            raw[c] = (row < M && ch < nch) ? __ldcs(src + ch) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    uint4 raw[CH];
+    load(blockIdx.x, raw);
+    int k = 0;
+    for (int64_t row = blockIdx.x; row < M; row += gridDim.x, ++k) {
+        float v[CH * 8];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const uint32_t u[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[8 * c + 2 * j] = bf16_lo(u[j]);
+                v[8 * c + 2 * j + 1] = bf16_hi(u[j]);
+            }
+        }
+        if constexpr (COLSCALE) {
+#pragma unroll
+            for (int i = 0; i < CH * 4; ++i) {
+                v[2 * i] = round_bf16(__fmul_rn(v[2 * i], bf16_lo(csb[i])));
+                v[2 * i + 1] = round_bf16(__fmul_rn(v[2 * i + 1], bf16_hi(csb[i])));
+            }
+        }
+        load(row + gridDim.x, raw);  // the next row's loads fly meanwhile
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < CH * 8; i += 2) amax = max3_abs(amax, v[i], v[i + 1]);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        if ((t & 31) == 0) red[k & 1][t >> 5] = amax;
+        __syncthreads();
+        const float rm = fmaxf(fmaxf(red[k & 1][0], red[k & 1][1]), fmaxf(red[k & 1][2], red[k & 1][3]));
+        float s;
+        const float y = row_scale_inv(rm, s);
+        if (t == 0) scale[row] = s;
+        int8_t *qr = q + row * K;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int ch = t + 128 * c;
+            if (ch < nch) {
+                uint32_t b[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    // |x / s| <= 127 (+ulps): the magic sum's low byte is rint(x / s)
+                    b[j] = __float_as_uint(__fadd_rn(div_by_rcp(v[8 * c + j], s, y), 12582912.0f)) & 0xFFu;
+                }
+                uint2 o;
+                o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+                o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+                __stcs(reinterpret_cast<uint2 *>(qr + 8 * ch), o);
+            }
+        }
     }
 }
 
@@ -115,7 +214,11 @@ __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict
 
 __global__ void colscale_kernel(float *tg, int64_t N) {
     const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (n < N) tg[n] = fmaxf(__fdiv_rn(tg[n], 127.0f), 1e-30f);
+    if (n < N) {
+        float s;
+        row_scale_inv(tg[n], s);
+        tg[n] = s;
+    }
 }
 
 __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restrict__ dy,
@@ -138,8 +241,9 @@ __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restric
         uint32_t b[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            b[2 * j] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j]));
-            b[2 * j + 1] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1]));
+            b[2 * j] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], rcp_rn(t[2 * j])));
+            b[2 * j + 1] = static_cast<uint8_t>(
+                q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], rcp_rn(t[2 * j + 1])));
         }
         uint2 o;
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
@@ -148,6 +252,28 @@ __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restric
     }
 }
 
+}  // namespace
+
+namespace {
+// resident CTAs per SM of a kernel (no dynamic shared memory), cached per kernel
+template <typename Kern>
+int resident_per_sm(Kern kern, int threads) {
+    struct Entry {
+        const void *fn;
+        int per;
+    };
+    static Entry cache[32] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    const void *fn = reinterpret_cast<const void *>(kern);
+    int i = 0;
+    for (; i < 32 && cache[i].fn; ++i)
+        if (cache[i].fn == fn) return cache[i].per;
+    int per = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, threads, 0) != cudaSuccess || per < 1) per = 1;
+    if (i < 32) cache[i] = {fn, per};
+    return per;
+}
 }  // namespace
 
 int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, int8_t *q,
@@ -164,6 +290,34 @@ int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, i
         return 2;
     }
     const uint16_t *xb = static_cast<const uint16_t *>(x);
+    const int64_t nch = K / 8;
+    const int ch = static_cast<int>((nch + 127) / 128);
+    if (ch <= 8) {
+        // persistent CTAs: as many as are resident at once, at most one per row
+        auto go = [&](auto kern, const float *c) {
+            const int per = resident_per_sm(kern, 128);
+            const int64_t grid = std::min<int64_t>(M, static_cast<int64_t>(num_sms()) * per);
+            kern<<<static_cast<unsigned>(grid), 128, 0, s>>>(xb, c, q, scale, M, K);
+        };
+#define XPU_RQ_CASE(C)                                                     \
+    case C:                                                                \
+        if (col_scale) go(quantize_row_reg_kernel<true, C>, col_scale);    \
+        else go(quantize_row_reg_kernel<false, C>, nullptr);               \
+        break;
+        switch (ch) {
+            XPU_RQ_CASE(1)
+            XPU_RQ_CASE(2)
+            XPU_RQ_CASE(3)
+            XPU_RQ_CASE(4)
+            XPU_RQ_CASE(5)
+            XPU_RQ_CASE(6)
+            XPU_RQ_CASE(7)
+            XPU_RQ_CASE(8)
+            default: break;
+        }
+#undef XPU_RQ_CASE
+        return launch_status("quantize_row");
+    }
     if (col_scale)
         quantize_row_kernel<true><<<static_cast<unsigned>(M), 256, 0, s>>>(xb, col_scale, q, scale, K);
     else

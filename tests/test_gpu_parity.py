@@ -120,14 +120,16 @@ def test_quantize_edge_rows():
 
 def test_scale_math_matches_the_ieee_definition():
     """The quantizers' row scale (s = max(amax/127, 1e-30), 1/s) without the
-    library divide equals the IEEE form on every non-negative float, and the
-    packed code arithmetic rounds the product and the sum separately."""
+    library divide equals the IEEE form on every non-negative float, the packed
+    code arithmetic rounds the product and the sum separately, and the row
+    quantizer's division gives the IEEE division's code on every pair of bf16
+    value and bf16 row maximum."""
     import ctypes
     from xpu_kernels.int8 import _lib as L
     bad_scale, bad_quant = ctypes.c_int64(-1), ctypes.c_int64(-1)
     rc = L.load().xpuint8_check_scale_math(ctypes.addressof(bad_scale), ctypes.addressof(bad_quant))
     assert rc == 0, L.load().xpuint8_last_error()
-    assert (bad_scale.value, bad_quant.value) == (0, 0)
+    assert (bad_scale.value, bad_quant.value) == (0, 0), L.load().xpuint8_last_error()
 
 
 def test_quantize_full_c5_every_code():
