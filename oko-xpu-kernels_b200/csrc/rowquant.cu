@@ -12,8 +12,10 @@
 //
 // colquant: the operand of the int8 weight gradient.  g[m,n] = dy[m,n]*xs[m]
 //   (fp32), per-column tg[n] = max(amax_m |g| / 127, 1e-30),
-//   gq[m,n] = clamp(rint(g / tg[n]), +-127).  Three launches: column abs-max
-//   (atomicMax on the bit pattern of a non-negative float), scale, quantize.
+//   gq[m,n] = clamp(rint(g / tg[n]), +-127).  Three launches over tiles of
+//   128 rows x 256 columns: column abs-max (reduced per tile in shared memory,
+//   then one atomicMax per column on the bit pattern of a non-negative
+//   float), scale, quantize.
 //
 // Division.  Every x / s is RN(x / s) computed as Markstein's correction of
 // the product with the correctly rounded reciprocal y = RN(1 / s) (Markstein,
@@ -188,31 +190,55 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
     }
 }
 
-// column abs-max of g = dy * xs over a strip of rows; 8 columns per thread
+// Column quantizer tiles: a 256-thread CTA covers kColRows rows x 256
+// columns; thread (ty, tx) = (threadIdx.x / 32, threadIdx.x % 32) owns the 8
+// columns 8 tx .. 8 tx + 7 of the tile and the rows ty, ty + 8, ... of it, so
+// a warp reads 512 contiguous bytes of a row and keeps four loads in flight.
+constexpr int kColRows = 128;
+
+// column abs-max of g = dy * xs: a CTA reduces its tile over rows in shared
+// memory and posts one atomicMax per column (on the bit pattern of a
+// non-negative float)
 __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict__ dy,
                                                       const float *__restrict__ xs,
                                                       unsigned int *__restrict__ amax,
-                                                      int64_t M, int64_t N, int rows_per_cta) {
-    const int64_t n = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
-    if (n >= N) return;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * rows_per_cta;
-    const int64_t m1 = min(M, m0 + rows_per_cta);
+                                                      int64_t M, int64_t N) {
+    __shared__ float red[8][256];
+    pdl_wait();
+    pdl_trigger();
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + 8 * tx;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kColRows;
+    const int64_t m1 = min(M, m0 + kColRows);
     float mx[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int64_t m = m0; m < m1; ++m) {
-        const float x = __ldg(xs + m);
-        const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+    if (n < N) {
+#pragma unroll 4
+        for (int64_t m = m0 + ty; m < m1; m += 8) {
+            const float x = __ldg(xs + m);
+            const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            mx[2 * j] = fmaxf(mx[2 * j], fabsf(__fmul_rn(bf16_lo(u[j]), x)));
-            mx[2 * j + 1] = fmaxf(mx[2 * j + 1], fabsf(__fmul_rn(bf16_hi(u[j]), x)));
+            for (int j = 0; j < 4; ++j) {
+                mx[2 * j] = fmaxf(mx[2 * j], fabsf(__fmul_rn(bf16_lo(u[j]), x)));
+                mx[2 * j + 1] = fmaxf(mx[2 * j + 1], fabsf(__fmul_rn(bf16_hi(u[j]), x)));
+            }
         }
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) atomicMax(amax + n + t, __float_as_uint(mx[t]));
+    for (int t = 0; t < 8; ++t) red[ty][8 * tx + t] = mx[t];
+    __syncthreads();
+    const int64_t c = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (c < N) {
+        float v = red[0][threadIdx.x];
+#pragma unroll
+        for (int r = 1; r < 8; ++r) v = fmaxf(v, red[r][threadIdx.x]);
+        atomicMax(amax + c, __float_as_uint(v));
+    }
 }
 
 __global__ void colscale_kernel(float *tg, int64_t N) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (n < N) {
         float s;
@@ -221,29 +247,39 @@ __global__ void colscale_kernel(float *tg, int64_t N) {
     }
 }
 
+// gq = clamp(rint(g / tg[n]), +-127), g = dy * xs; each thread's 8 column
+// reciprocals are computed once
 __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restrict__ dy,
                                                        const float *__restrict__ xs,
                                                        const float *__restrict__ tg,
                                                        int8_t *__restrict__ gq, int64_t M,
                                                        int64_t N) {
-    const int64_t chunks = N >> 3;
-    const int64_t total = M * chunks;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t m = i / chunks;
-        const int64_t n = (i - m * chunks) << 3;
-        const float x = __ldg(xs + m);
-        const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
+    pdl_wait();
+    pdl_trigger();
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + 8 * tx;
+    if (n >= N) return;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kColRows;
+    const int64_t m1 = min(M, m0 + kColRows);
+    float t[8], y[8];
+    {
         const float4 t0 = __ldg(reinterpret_cast<const float4 *>(tg + n));
         const float4 t1 = __ldg(reinterpret_cast<const float4 *>(tg + n) + 1);
-        const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+        t[0] = t0.x; t[1] = t0.y; t[2] = t0.z; t[3] = t0.w;
+        t[4] = t1.x; t[5] = t1.y; t[6] = t1.z; t[7] = t1.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = rcp_rn(t[j]);
+    }
+#pragma unroll 4
+    for (int64_t m = m0 + ty; m < m1; m += 8) {
+        const float x = __ldg(xs + m);
+        const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
         const uint32_t u[4] = {w.x, w.y, w.z, w.w};
         uint32_t b[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            b[2 * j] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], rcp_rn(t[2 * j])));
-            b[2 * j + 1] = static_cast<uint8_t>(
-                q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], rcp_rn(t[2 * j + 1])));
+            b[2 * j] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], y[2 * j]));
+            b[2 * j + 1] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], y[2 * j + 1]));
         }
         uint2 o;
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
@@ -328,19 +364,34 @@ int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, i
 int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t *gq, float *tg,
                     int64_t M, int64_t N) {
     const uint16_t *d = static_cast<const uint16_t *>(dy);
+    if ((M + kColRows - 1) / kColRows > 65535) {
+        set_error("M is too large for the column quantizer");
+        return 2;
+    }
     if (cudaMemsetAsync(tg, 0, static_cast<size_t>(N) * sizeof(float), s) != cudaSuccess)
         return launch_status("colquant memset");
-    const int rows_per_cta = 64;
-    dim3 grid1(static_cast<unsigned>((N / 8 + 255) / 256),
-               static_cast<unsigned>((M + rows_per_cta - 1) / rows_per_cta));
-    colamax_kernel<<<grid1, 256, 0, s>>>(d, x_scale, reinterpret_cast<unsigned int *>(tg), M, N,
-                                          rows_per_cta);
-    colscale_kernel<<<static_cast<unsigned>((N + 255) / 256), 256, 0, s>>>(tg, N);
-    const int64_t total = M * (N >> 3);
-    int64_t blocks = (total + 255) / 256;
-    const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
-    if (blocks > cap) blocks = cap;
-    colquant_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, x_scale, tg, gq, M, N);
+    const dim3 grid(static_cast<unsigned>((N + 255) / 256), static_cast<unsigned>((M + kColRows - 1) / kColRows));
+    // the three kernels launch with programmatic serialization (each waits
+    // for the one before it before touching memory)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(256);
+    cfg.gridDim = grid;
+    unsigned int *amax = reinterpret_cast<unsigned int *>(tg);
+    if (cudaLaunchKernelEx(&cfg, colamax_kernel, d, x_scale, amax, M, N) != cudaSuccess)
+        return launch_status("colquant (column maxima)");
+    cfg.gridDim = dim3(static_cast<unsigned>((N + 255) / 256));
+    if (cudaLaunchKernelEx(&cfg, colscale_kernel, tg, N) != cudaSuccess)
+        return launch_status("colquant (scales)");
+    cfg.gridDim = grid;
+    if (cudaLaunchKernelEx(&cfg, colquant_kernel, d, x_scale, static_cast<const float *>(tg), gq, M, N) !=
+        cudaSuccess)
+        return launch_status("colquant");
     return launch_status("colquant");
 }
 

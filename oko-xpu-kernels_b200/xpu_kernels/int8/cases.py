@@ -3,6 +3,7 @@
     python -m xpu_kernels.int8.cases gemm --M 2048 --N 10240 --K 1280 --iters 20
     python -m xpu_kernels.int8.cases rotate_quant --M 65536 --K 4096
     python -m xpu_kernels.int8.cases linear | ffn | dx | dw | quantize_row | dequant
+    python -m xpu_kernels.int8.cases suite [--iters N]   (every shape of SUITE)
 
 Inputs are seeded and generated on the device; each case launches its kernel
 `--iters` times over `--sets` rotating buffer sets and prints the average
@@ -35,7 +36,33 @@ def _time(fn, iters, stream):
     return e0.elapsed_time(e1) / iters
 
 
+# The shapes the committed ncu summaries cover (BASELINE configs C3 W1, C3
+# GEGLU, C4 backward, C5), run by ``cases suite`` in one process: each case
+# launches its kernels ``--iters`` times (profile with a kernel-name filter).
+SUITE = [
+    ["gemm", "--M", "2048", "--N", "10240", "--K", "1280", "--sets", "6"],
+    ["geglu", "--M", "2048", "--N", "5120", "--K", "1280", "--sets", "6"],
+    ["gemm", "--M", "8192", "--N", "14336", "--K", "4096", "--sets", "1"],
+    ["gemm_nn", "--M", "4096", "--N", "1280", "--K", "5120", "--sets", "2"],
+    ["gemm_tn", "--M", "5120", "--N", "1280", "--K", "4096", "--sets", "2"],
+    ["rotate_quant", "--M", "65536", "--K", "4096", "--sets", "1"],
+    ["rotate_quant", "--M", "2048", "--K", "1280", "--sets", "8"],
+    ["rotate", "--M", "65536", "--K", "4096", "--sets", "1"],
+    ["quantize_row", "--M", "4096", "--K", "5120", "--sets", "2"],
+    ["dequant", "--M", "16384", "--N", "14336", "--sets", "1"],
+    ["dequant_act", "--M", "2048", "--K", "5120", "--sets", "2"],
+    ["dw", "--M", "4096", "--N", "5120", "--K", "1280"],
+]
+
+
 def main(argv=None):
+    import sys
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if argv and argv[0] == "suite":
+        iters = argv[argv.index("--iters") + 1] if "--iters" in argv else "2"
+        for case in SUITE:
+            main(case + ["--iters", iters])
+        return
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "gemm_raw", "gemm_nn", "gemm_tn", "geglu",
                                      "rotate_quant", "rotate", "linear", "ffn", "dx", "dw",

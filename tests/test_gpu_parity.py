@@ -381,7 +381,7 @@ def test_quantize_row_matches_the_reference_fixture():
     assert bits(q)[0, :4].tolist() == [64, 127, -127, 32]
 
 
-@pytest.mark.parametrize("m,k", [(64, 5120), (3, 24), (100, 1000)])
+@pytest.mark.parametrize("m,k", [(64, 5120), (3, 24), (100, 1000), (40, 8192), (7, 8200)])
 def test_quantize_row_is_bit_exact(m, k):
     from xpu_kernels import int8
     x = rand_bf16((m, k), 140 + k, scale=1e-3)
@@ -391,6 +391,37 @@ def test_quantize_row_is_bit_exact(m, k):
     assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
     qt, st = int8.quantize_row_torch(x.to(DEV))
     assert torch.equal(qt.cpu(), torch.from_numpy(qr))
+
+
+@pytest.mark.parametrize("m,k", [(33, 5120), (5, 1032), (9, 8200)])
+def test_quantize_row_column_scaled_is_bit_exact(m, k):
+    """bf16(x * bf16(col_scale)) then the row quantizer (linear_dx_int8's operand)."""
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 160 + k, scale=1e-3)
+    cs = torch.rand(k, generator=torch.Generator().manual_seed(k)) * 0.04 + 1e-4
+    q, s = int8.quantize_row(x.to(DEV), cs.to(DEV))
+    d = O.f32_to_bf16_bits(O.bf16_bits_to_f32(bits(x)) * O.round_bf16(cs.numpy().astype(np.float32)))
+    qr, sr = O.quantize_row(d)
+    assert np.array_equal(bits(q), qr)
+    assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n", [(1000, 5136), (3, 16), (129, 272)])
+def test_colquant_is_bit_exact(m, n):
+    """The int8 weight gradient's column quantizer on ragged tiles."""
+    import ctypes
+    from xpu_kernels.int8 import _lib as L
+    dy = rand_bf16((m, n), 170 + n, scale=1e-3)
+    xs = (torch.rand(m, generator=torch.Generator().manual_seed(m)) * 0.05 + 1e-3).float()
+    gq = torch.empty(m, n, dtype=torch.int8, device=DEV)
+    tg = torch.empty(n, dtype=torch.float32, device=DEV)
+    dyd, xsd = dy.to(DEV), xs.to(DEV)
+    rc = L.load().xpuint8_colquant_stream(L._stream(torch.device(DEV)), L._ptr(dyd), L._ptr(xsd),
+                                          L._ptr(gq), L._ptr(tg), m, n)
+    assert rc == 0, L.load().xpuint8_last_error()
+    qr, tr = O.colquant_scaled(bits(dy), xs.numpy())
+    assert np.array_equal(bits(tg).view(np.uint32), tr.view(np.uint32))
+    assert np.array_equal(bits(gq), qr)
 
 
 def test_linear_dx_int8_matches_the_oracle():
