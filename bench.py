@@ -465,15 +465,102 @@ def _rank0_extras(args, lib, L, dev, sets, stream):
     return out
 
 
+def run_nshard(args):
+    """Config C5's N-sharded variant (not the headline): x [M, 4096] on every
+    rank, W [14336, 4096] split by output channels, the output all-gathered to
+    every rank.  Times the fused form (the GEMM stores its tiles into every
+    rank's buffer over NVLink) and the NCCL form (GEMM, all-gather, strided
+    copy); whole-job TOPS = 2*M*N*K / time (max over ranks): strong scaling."""
+    import datetime
+    import torch.distributed as dist
+    import xpu_kernels
+    from xpu_kernels.int8 import shard
+
+    ws_, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws_ > 1:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    m, k, n = args.nshard_m, 4096, 14336
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn(m, k, generator=g, device=dev)
+    x[:, :20] *= 20
+    x = x.to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w8, wsc = xpu_kernels.prepare_weight(w)
+    del w
+    w8l, wsl, _ = shard.shard_weight(w8, wsc, ws_, rank)
+    out = shard.PeerOutput(m, n) if ws_ > 1 else None
+    stream = torch.cuda.current_stream(dev)
+
+    def fused():
+        if out is None:
+            return xpu_kernels.linear(x, w8l, wsl)
+        return shard.linear_nshard_fused(x, w8l, wsl, None, out)
+
+    def nccl():
+        if ws_ == 1:
+            return xpu_kernels.linear(x, w8l, wsl)
+        return shard.linear_nshard(x, w8l, wsl, None, n_total=n)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        if ws_ > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+        if ws_ > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # the two forms agree bit for bit
+    y_f = fused().clone()
+    y_n = nccl()
+    same = bool(torch.equal(y_f.view(torch.int16), y_n.view(torch.int16)))
+    t_f = timed(fused)
+    t_n = timed(nccl)
+    ops_ = 2.0 * m * n * k
+    if out is not None:
+        out.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"ConvRot int8 linear N-sharded TOPS @M={m},K={k},N={n}",
+            "value": ops_ / (t_f * 1e-3) / 1e12, "unit": "TOPS", "n_gpus": ws_,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_f,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {"workload": "config C5 N-sharded variant", "M": m,
+                                            "K": k, "N": n, "parallelism": f"N-shard x{ws_}"},
+            "fused_allgather_ms": t_f, "nccl_allgather_ms": t_n,
+            "nccl_tops": ops_ / (t_n * 1e-3) / 1e12, "forms_bit_identical": same,
+            "output_bytes_per_rank_sent": m * (n // ws_) * 2 * (ws_ - 1)}))
+    if ws_ > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--mode", choices=("linear", "nshard"), default="linear",
+                    help="linear: the headline (config C3 W1, M-sharded); nshard: config C5's "
+                         "N-sharded variant with the output all-gather")
+    ap.add_argument("--nshard-m", type=int, default=65536)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "nshard":
+        return run_nshard(args)
     return run_gpu(args)
 
 

@@ -165,6 +165,35 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
  * device synchronisation; reset != 0 clears it. */
 int xpuint8_fault_status(int32_t reset);
 
+/* The N-sharded INT8 linear with its output all-gather fused into the GEMM
+ * (BASELINE config C5's large-weight variant; the reference has no
+ * distributed code).  Rank `rank` of `nranks` holds weight rows
+ * [rank*N, (rank+1)*N) (w8 [N,K] int8, w_scale [N] fp32, bias [N] or NULL)
+ * and the whole activation x [M,K] bf16; outs[r] is rank r's output
+ * [M, nranks*N] bf16 as mapped in this process (its own buffer and the
+ * peers' through xpuint8_ipc_open).  Every output tile of this rank's
+ * block is written by the TMA unit into all nranks buffers at columns
+ * [rank*N, (rank+1)*N), over NVLink as the tiles finish.  xq [M,K] int8 and
+ * xs [M] fp32 are caller scratch.  The caller orders the ranks around the
+ * call: every rank's previous readers of its output before, every rank's
+ * call before readers after (a device-side barrier such as a one-element
+ * all-reduce on the same stream).  nranks <= 8, N % 16 == 0, K % 256 == 0. */
+int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int8_t *w8,
+                                    const float *w_scale, const float *bias, void *const *outs,
+                                    int32_t nranks, int32_t rank, int8_t *xq, float *xs, int64_t M,
+                                    int64_t N, int64_t K, int32_t activation);
+
+/* Peer-visible device buffers for the fused all-gather (set-up time, not per
+ * call): xpuint8_ipc_alloc allocates `bytes` on the current device and
+ * writes its 64-byte CUDA IPC handle; another process opens it with
+ * xpuint8_ipc_open (a mapping valid on its current device, peer access
+ * enabled lazily), releases the mapping with xpuint8_ipc_close; the owner
+ * frees with xpuint8_ipc_free.  No counterpart in the reference. */
+int xpuint8_ipc_alloc(int64_t bytes, void **ptr, void *handle);
+int xpuint8_ipc_open(const void *handle, void **ptr);
+int xpuint8_ipc_close(void *ptr);
+int xpuint8_ipc_free(void *ptr);
+
 /* Self-check of the quantizers' scale arithmetic (blocking, default stream):
  * the fast row scale s = max(amax/127, 1e-30) and 1/s against the IEEE
  * divide / reciprocal on every non-negative float, and the packed

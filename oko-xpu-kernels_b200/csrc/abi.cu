@@ -501,6 +501,100 @@ int xpuint8_fault_status(int32_t reset) {
     return g != 0 ? g : r;
 }
 
+// ---------------------------------------------------------------- peer buffers
+int xpuint8_ipc_alloc(int64_t bytes, void **ptr, void *handle) {
+    if (bytes <= 0 || !ptr || !handle) {
+        set_error("ipc_alloc: a positive size and non-null ptr / handle are required");
+        return 2;
+    }
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+    if (e != cudaSuccess) {
+        set_error(std::string("ipc_alloc: cudaMalloc: ") + cudaGetErrorString(e));
+        return 5;
+    }
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_error(std::string("ipc_alloc: cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+        return 5;
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return 0;
+}
+
+int xpuint8_ipc_open(const void *handle, void **ptr) {
+    if (!handle || !ptr) {
+        set_error("ipc_open: handle and ptr must not be null");
+        return 2;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        set_error(std::string("ipc_open: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+        return 5;
+    }
+    *ptr = p;
+    return 0;
+}
+
+int xpuint8_ipc_close(void *ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) {
+        set_error(std::string("ipc_close: ") + cudaGetErrorString(e));
+        return 5;
+    }
+    return 0;
+}
+
+int xpuint8_ipc_free(void *ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) {
+        set_error(std::string("ipc_free: ") + cudaGetErrorString(e));
+        return 5;
+    }
+    return 0;
+}
+
+int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int8_t *w8,
+                                    const float *w_scale, const float *bias, void *const *outs,
+                                    int32_t nranks, int32_t rank, int8_t *xq, float *xs, int64_t M,
+                                    int64_t N, int64_t K, int32_t activation) {
+    if (N <= 0 || N % 16 != 0) {
+        set_error("N (this rank's columns) must be a positive multiple of 16");
+        return 2;
+    }
+    if (!outs || nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) {
+        set_error("allgather: 1 <= nranks <= 8, 0 <= rank < nranks and an output table are required");
+        return 2;
+    }
+    void *dst[8];
+    for (int r = 0; r < nranks; ++r) {
+        if (!outs[r] || !aligned16(outs[r])) {
+            set_error("allgather: every output buffer needs a 16-byte aligned base");
+            return 2;
+        }
+        // this rank's column block of rank r's [M, nranks * N] output
+        dst[r] = static_cast<char *>(outs[r]) + static_cast<int64_t>(rank) * N * 2;
+    }
+    if (!w8 || !w_scale || !aligned16(w8)) {
+        set_error("a required pointer is null or misaligned");
+        return 2;
+    }
+    if (int rc = convrot_quantize(as_stream(stream), x, xq, xs, M, K, activation)) return rc;
+    GemmCall c;
+    c.epilogue = kEpiDequantBf16;
+    c.a = xq; c.b = w8; c.lda = K; c.ldb = K;
+    c.outs = dst; c.nout = nranks; c.ldo = static_cast<int64_t>(nranks) * N;
+    c.row_scale = xs; c.col_scale = w_scale; c.bias = bias;
+    c.M = M; c.N = N; c.K = K;
+    return launch_gemm(as_stream(stream), c);
+}
+
 int xpuint8_check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {
     if (!bad_scale || !bad_quant) {
         set_error("a required pointer is null");

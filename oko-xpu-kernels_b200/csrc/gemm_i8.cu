@@ -75,6 +75,16 @@ struct GemmArgs {
     // num_m counts 256-row pair tiles
 };
 
+// The output's tensor maps: one per destination.  Every output tile is
+// stored to each of them (the N-sharded linear's all-gather: this rank's
+// column block into every rank's output, peers' buffers mapped by CUDA IPC
+// and written over NVLink by the TMA unit, tile by tile as the tiles finish).
+constexpr int kMaxOut = 8;
+struct OutMaps {
+    CUtensorMap m[kMaxOut];
+    int n;
+};
+
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int &mb, int &nb) {
     const int per_group = GROUP_M * num_n;
     const int group = tile / per_group;
@@ -136,12 +146,16 @@ __device__ __forceinline__ void stage_bf16_32(uint32_t buf, int lane, const floa
                      cvt_bf16x2(v[8 * c + 6], v[8 * c + 7]));
 }
 
-// hand a filled buffer to the TMA unit (one lane), then flip buffers
-__device__ __forceinline__ void stage_flush(const void *tmap, uint32_t buf, int lane, int x, int y) {
+// hand a filled buffer to the TMA unit (one lane: a store per destination,
+// one bulk group), then flip buffers
+__device__ __forceinline__ void stage_flush(const OutMaps &om, uint32_t buf, int lane, int x, int y) {
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(tmap, buf, x, y);
+        tma_store_2d(&om.m[0], buf, x, y);
+#pragma unroll
+        for (int i = 1; i < kMaxOut; ++i)
+            if (i < om.n) tma_store_2d(&om.m[i], buf, x, y);
         bulk_commit();
     }
 }
@@ -207,7 +221,7 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
 // Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
 // quarter) x columns [c0, c1), 32 columns at a time.
 template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmOut, uint32_t taddr,
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &tmOut, uint32_t taddr,
                                               int m0, int n0, int quarter, int c0, int c1, int lane,
                                               float xs, const float *s_ws, const float *s_b,
                                               uint32_t bufs, int &bsel) {
@@ -256,7 +270,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const void *tmO
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
+                   const __grid_constant__ OutMaps tmOut, const GemmArgs args) {
     constexpr int STAGES = Cfg<EPI>::kStages;
     constexpr int kEpiWarps = Cfg<EPI>::kEpiWarps;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -302,7 +316,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
-        prefetch_tmap(&tmOut);
+        for (int i = 0; i < tmOut.n; ++i) prefetch_tmap(&tmOut.m[i]);
     }
     // both CTAs' barriers exist before either CTA arrives on the other's
     cluster_sync();
@@ -466,7 +480,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             tc_fence_after();
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
-            epilogue_tile<EPI>(args, &tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
+            epilogue_tile<EPI>(args, tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
                                s_b, bufs, bsel);
             // hand the accumulator back to the leader's MMA issuer (one arrival per warp)
             tc_fence_before();
@@ -567,7 +581,7 @@ int resident_pairs(int dev) {
 }
 
 template <int EPI, bool A_MN, bool B_MN>
-int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
+int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const OutMaps &mo,
                 const GemmArgs &a, int pairs) {
     auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     cudaLaunchConfig_t cfg = {};
@@ -592,7 +606,7 @@ int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, co
 
 template <int EPI, bool A_MN, bool B_MN>
 int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
-                 const CUtensorMap &mo, const GemmArgs &a, int64_t tiles) {
+                 const OutMaps &mo, const GemmArgs &a, int64_t tiles) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int resident = resident_pairs<EPI, A_MN, B_MN>(dev);
@@ -624,7 +638,7 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("the GEGLU epilogue needs K-major operands");
         return 2;
     }
-    const uintptr_t oa = reinterpret_cast<uintptr_t>(c.out);
+    const uintptr_t oa = reinterpret_cast<uintptr_t>(c.outs ? c.outs[0] : c.out);
     if ((oa & 15u) || (c.ldo % 8)) {
         set_error("the output needs a 16-byte aligned base and a row stride multiple of 8");
         return 2;
@@ -675,16 +689,30 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     } else {
         if (!make_map(&mb, c.b, c.N, c.K, c.ldb, 128, BK)) return 2;
     }
-    // output: 32-row boxes, 64-byte rows (16 int32 or 32 bf16 columns), 64-byte swizzle
-    CUtensorMap mo;
-    if (c.epilogue == kEpiRawI32) {
-        if (!make_map(&mo, c.out, c.N, c.M, c.ldo * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_INT32,
-                      CU_TENSOR_MAP_SWIZZLE_64B))
+    // output: 32-row boxes, 64-byte rows (16 int32 or 32 bf16 columns), 64-byte
+    // swizzle; one map per destination (c.out, or the c.nout buffers of c.outs)
+    OutMaps mo{};
+    const int nout = c.outs ? c.nout : 1;
+    if (nout < 1 || nout > kMaxOut) {
+        set_error("between 1 and 8 output buffers");
+        return 2;
+    }
+    mo.n = nout;
+    for (int i = 0; i < nout; ++i) {
+        void *base = c.outs ? c.outs[i] : c.out;
+        if (!base || (reinterpret_cast<uintptr_t>(base) & 15u)) {
+            set_error("every output buffer needs a 16-byte aligned base");
             return 2;
-    } else {
-        if (!make_map(&mo, c.out, c.N, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                      CU_TENSOR_MAP_SWIZZLE_64B))
-            return 2;
+        }
+        if (c.epilogue == kEpiRawI32) {
+            if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_INT32,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+                return 2;
+        } else {
+            if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          CU_TENSOR_MAP_SWIZZLE_64B))
+                return 2;
+        }
     }
     GemmArgs a{};
     a.out = c.out; a.ldo = c.ldo;

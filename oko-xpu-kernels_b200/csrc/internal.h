@@ -49,6 +49,8 @@ struct GemmCall {
     int64_t lda = 0, ldb = 0;
     void *out = nullptr;        // int32 or bf16 [M, N], row stride ldo (elements)
     int64_t ldo = 0;
+    void *const *outs = nullptr;  // instead of out: nout destinations, each tile stored to all
+    int nout = 0;
     const float *row_scale = nullptr;  // [M]  (x_scale)
     const float *col_scale = nullptr;  // [N]  (w_scale) or null = 1; GEGLU: [2N]
     const float *bias = nullptr;       // [N]  or null

@@ -78,6 +78,11 @@ def _signatures():
         "xpuint8_colquant_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_fault_status": [i32],
         "xpuint8_check_scale_math": [vp, vp],
+        "xpuint8_linear_allgather_stream": [vp] * 6 + [i32, i32, vp, vp] + [i64] * 3 + [i32],
+        "xpuint8_ipc_alloc": [i64, vp, vp],
+        "xpuint8_ipc_open": [vp, vp],
+        "xpuint8_ipc_close": [vp],
+        "xpuint8_ipc_free": [vp],
         "xpuint8_linear_noalloc_stream": [vp] * 6 + [i64] * 3 + [i32],
     }
 

@@ -11,9 +11,17 @@ two ways:
 * **N-sharding** (config C5's variant for the large weight): rank r owns the
   weight rows ``col_range(N, P, r)`` (output columns) and the whole activation,
   computes ``y_r = linear(x, w8_r, ws_r)`` ([M, N/P]) and the ranks all-gather
-  the column blocks into the full ``[M, N]`` (:func:`gather_columns`).  The
-  gather is NCCL over NVLink; each rank's GEMM writes its block contiguously
-  and the assembly into row-major ``[M, N]`` is one strided copy.
+  the column blocks into the full ``[M, N]``.  Two forms:
+
+  - :func:`linear_nshard_fused`: the GEMM's epilogue stores every output tile
+    of this rank's block straight into every rank's ``[M, N]`` buffer
+    (:class:`PeerOutput`, mapped across the processes with CUDA IPC) over
+    NVLink, so the exchange overlaps the GEMM tile by tile and lands in
+    row-major order; two one-element all-reduces on the stream order the
+    ranks around it;
+  - :func:`linear_nshard`: the GEMM, then an NCCL all-gather of the blocks
+    (:func:`gather_columns`) and a strided copy into row-major ``[M, N]`` (the
+    form that runs on any backend, e.g. gloo on CPU).
 """
 
 from __future__ import annotations
@@ -23,7 +31,7 @@ from typing import Callable, Optional, Tuple
 import torch
 
 __all__ = ["row_range", "col_range", "split_rows", "shard_weight", "linear_mshard",
-           "gather_columns", "linear_nshard"]
+           "gather_columns", "linear_nshard", "PeerOutput", "linear_nshard_fused"]
 
 
 def _balanced(n: int, parts: int, index: int, align: int = 1) -> Tuple[int, int]:
@@ -115,3 +123,126 @@ def linear_nshard(x, w8_local, w_scale_local, bias_local=None, n_total: Optional
     y = linear(x, w8_local, w_scale_local, bias_local)
     return gather_columns(y.reshape(-1, y.shape[-1]), n_total, group).reshape(
         *x.shape[:-1], n_total)
+
+
+class _CudaBuffer:
+    """A raw device allocation seen through ``__cuda_array_interface__`` (int16
+    elements; viewed as bf16 by the caller)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape),
+                                         "typestr": "<i2", "version": 3, "strides": None}
+
+
+class PeerOutput:
+    """The all-gathered output of :func:`linear_nshard_fused`: a bf16 buffer
+    ``[m, n_total]`` on every rank of ``group``, mapped into every other rank's
+    process (CUDA IPC), so that each rank's GEMM can store its column block into
+    all of them.  Collective: every rank constructs it with the same shape, on
+    its current CUDA device, and calls :meth:`close` when done.  ``tensor`` is
+    this rank's buffer (valid until the next call that writes it)."""
+
+    def __init__(self, m: int, n_total: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from ._lib import _lib
+
+        self._lib = _lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the fused all-gather supports at most 8 ranks")
+        self.m, self.n_total = int(m), int(n_total)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        if self._lib.xpuint8_ipc_alloc(self.m * self.n_total * 2, ctypes.byref(ptr), handle) != 0:
+            raise RuntimeError(f"PeerOutput: {self._lib.xpuint8_last_error()!r}")
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_char * 64).from_buffer_copy(h)
+            if self._lib.xpuint8_ipc_open(hb, ctypes.byref(p)) != 0:
+                raise RuntimeError(f"PeerOutput (rank {r}): {self._lib.xpuint8_last_error()!r}")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.table = (ctypes.c_void_p * self.world)(*ptrs)
+        self.tensor = torch.as_tensor(_CudaBuffer(self._own, (self.m, self.n_total)),
+                                      device=self.device).view(torch.bfloat16)
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank to do the same, free this
+        rank's buffer (collective)."""
+        import ctypes
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            self._lib.xpuint8_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.tensor = None
+        self._lib.xpuint8_ipc_free(ctypes.c_void_p(self._own))
+        self._own = None
+
+
+def _device_barrier(group, device):
+    """Orders every rank's earlier work on its stream before every rank's later
+    work (a one-element all-reduce on the current stream; no host wait)."""
+    import torch.distributed as dist
+    dist.all_reduce(torch.zeros(1, device=device), group=group)
+
+
+def linear_nshard_fused(x, w8_local, w_scale_local, bias_local, out: PeerOutput):
+    """The N-sharded INT8 linear with the all-gather fused into the GEMM: this
+    rank quantizes the whole activation, multiplies it by its block of output
+    channels and stores every output tile into all ranks' ``out`` buffers (the
+    TMA unit over NVLink), at this rank's columns.  Returns ``out.tensor[:M]``,
+    the full ``[M, N]`` output (rows of x beyond ``out.m`` are an error).
+
+    Collective over ``out.group``: every rank calls it with its own weight block
+    (equal blocks, ``N / P`` columns each).  Before the GEMM the ranks wait for
+    each other's readers of the previous output; after it, for each other's
+    stores.
+    """
+    from . import ops
+    from ._lib import _err, _lib, _ptr, _stream
+
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m, n = x2.shape[0], w8_local.shape[0]
+    reason = ops.unsupported_reason(x2, w8_local, w_scale_local)
+    if reason is not None:
+        raise TypeError(reason)
+    if n * out.world != out.n_total:
+        raise ValueError(f"{out.world} blocks of {n} columns do not make the output's {out.n_total}")
+    if m > out.m:
+        raise ValueError(f"{m} rows do not fit the output's {out.m}")
+    dev = x2.device
+    lib = _lib()
+    ws = ops.expand_scale(w_scale_local, n, dev)
+    b = None if bias_local is None else ops.expand_scale(bias_local, n, dev)
+    w8c = w8_local if w8_local.is_contiguous() else w8_local.contiguous()
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
+    _device_barrier(out.group, dev)
+    rc = lib.xpuint8_linear_allgather_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws), _ptr(b),
+                                             out.table, out.world, out.rank, _ptr(xq), _ptr(xs),
+                                             m, n, k, 0)
+    if rc != 0:
+        _err(lib, "linear_nshard_fused")
+    _device_barrier(out.group, dev)
+    return out.tensor[:m].reshape(*x.shape[:-1], out.n_total)

@@ -1,8 +1,11 @@
-"""The sharded INT8 linear on two GPUs (NCCL), bit for bit against one GPU.
+"""The sharded INT8 linear on two GPUs, bit for bit against one GPU.
 
 Rows are independent, so the M-sharded result of each rank must equal the
-single-GPU result on those rows exactly; the N-sharded all-gather must rebuild
-the single-GPU output exactly.  Skipped when fewer than two GPUs are visible.
+single-GPU result on those rows exactly; the N-sharded all-gather (NCCL, and
+the GEMM whose epilogue stores into the peers' buffers over NVLink) must
+rebuild the single-GPU output exactly.  Skipped when fewer than two GPUs are
+visible.  NVLS is off (NCCL_NVLS_ENABLE=0) and the fused path uses plain peer
+stores, no multicast.
 """
 
 import datetime
@@ -68,3 +71,51 @@ def test_sharded_linear_on_two_gpus(tmp_path):
         pass
     for r in range(world):
         assert (tmp_path / f"r{r}.txt").read_text() == "1 1"
+
+
+def _fused_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    import xpu_kernels
+    from xpu_kernels.int8 import shard
+    g = torch.Generator(device=dev).manual_seed(21)
+    k, n = 1280, 2048
+    w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w8, ws = xpu_kernels.prepare_weight(w)
+    bias = torch.randn(n, generator=g, device=dev) * 0.01
+    w8l, wsl, bl = shard.shard_weight(w8, ws, world, rank, bias)
+    out = shard.PeerOutput(1000, n)
+    oks = []
+    # two calls in a row (the second overwrites the first's output in every
+    # rank's buffer), a ragged row count, then fewer rows than the buffer holds
+    for m, seed in ((1000, 1), (1000, 2), (333, 3)):
+        gx = torch.Generator(device=dev).manual_seed(seed)
+        x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
+        full = xpu_kernels.linear(x, w8, ws, bias)
+        y = shard.linear_nshard_fused(x, w8l, wsl, bl, out)
+        torch.cuda.synchronize()
+        oks.append(int(torch.equal(y.view(torch.int16), full.view(torch.int16))))
+    from xpu_kernels.int8 import _lib as L
+    oks.append(int(L.load().xpuint8_fault_status(1) == 0))
+    out.close()
+    with open(os.path.join(outdir, f"f{rank}.txt"), "w") as f:
+        f.write(" ".join(map(str, oks)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_allgather_linear_on_two_gpus(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.start_processes(_fused_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                             join=False, start_method="spawn")
+    while not ctx.join(timeout=300):
+        pass
+    for r in range(world):
+        assert (tmp_path / f"f{r}.txt").read_text() == "1 1 1 1"
