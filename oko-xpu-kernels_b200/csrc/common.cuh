@@ -24,8 +24,19 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
     u += 0x7FFFu + ((u >> 16) & 1u);
     return u >> 16;
 }
+// fp32 -> bf16 -> fp32 through the hardware round-to-nearest-even conversion:
+// the bits of f32_to_bf16_bits for every non-NaN value (a NaN stays a NaN)
 __device__ __forceinline__ float round_bf16(float f) {
-    return __uint_as_float(f32_to_bf16_bits(f) << 16);
+    uint16_t h;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+    return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+// the same for two values with one conversion
+__device__ __forceinline__ void round_bf16x2(float &lo, float &hi) {
+    uint32_t p;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+    lo = __uint_as_float(p << 16);
+    hi = __uint_as_float(p & 0xFFFF0000u);
 }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);

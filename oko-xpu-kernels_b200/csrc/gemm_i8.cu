@@ -207,14 +207,15 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
                  mul2(mk2(wg.x, wg.y), xs2)), g0, g1);
         // h, g rounded to bf16 (the unfused chain stores them), then
         // y = bf16(h * bf16(0.5 g (1 + erf(g / sqrt 2))))
-        h0 = round_bf16(h0); h1 = round_bf16(h1);
-        g0 = round_bf16(g0); g1 = round_bf16(g1);
-        const float e0 = __fmul_rn(__fmul_rn(0.5f, g0),
-                                   __fadd_rn(1.0f, erff(__fmul_rn(g0, 0.7071067811865476f))));
-        const float e1 = __fmul_rn(__fmul_rn(0.5f, g1),
-                                   __fadd_rn(1.0f, erff(__fmul_rn(g1, 0.7071067811865476f))));
-        v[j] = __fmul_rn(h0, round_bf16(e0));
-        v[j + 1] = __fmul_rn(h1, round_bf16(e1));
+        round_bf16x2(h0, h1);
+        round_bf16x2(g0, g1);
+        float e0 = __fmul_rn(__fmul_rn(0.5f, g0),
+                             __fadd_rn(1.0f, erff(__fmul_rn(g0, 0.7071067811865476f))));
+        float e1 = __fmul_rn(__fmul_rn(0.5f, g1),
+                             __fadd_rn(1.0f, erff(__fmul_rn(g1, 0.7071067811865476f))));
+        round_bf16x2(e0, e1);
+        v[j] = __fmul_rn(h0, e0);
+        v[j + 1] = __fmul_rn(h1, e1);
     }
 }
 

@@ -542,8 +542,12 @@ __host__ __device__ constexpr int direct_depth(int mode, int) {
 #ifndef XPUINT8_DIRECT_CTAS
 #define XPUINT8_DIRECT_CTAS 5
 #endif
+#ifndef XPUINT8_QUANT_CTAS
+#define XPUINT8_QUANT_CTAS 7
+#endif
 constexpr int direct_min_ctas128(int mode, int act) {
-    return (mode == 0 && act_paired(act)) ? 4 : (direct_depth(mode, act) == 2 ? XPUINT8_DIRECT_CTAS : 8);
+    return (mode == 0 && act_paired(act)) ? 4
+                                          : (direct_depth(mode, act) == 2 ? XPUINT8_DIRECT_CTAS : XPUINT8_QUANT_CTAS);
 }
 
 // SLOTS half-warps per CTA (8 or 16): the row abs-max barrier spans one CTA,
