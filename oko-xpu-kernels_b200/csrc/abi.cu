@@ -185,9 +185,12 @@ int dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float 
 
 // layout: 0 = a [M,K], b [N,K] (a @ b^T); 1 = a [M,K], b [K,N] (a @ b);
 //         2 = a [K,M], b [K,N] (a^T @ b)
+// b_early: the kernel launched just before on `s` is this library's activation
+// quantizer (or does not write b, col_scale, bias), so the GEMM may load those
+// before it completes
 int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, void *out,
                   const float *row_scale, const float *col_scale, const float *bias, int64_t M,
-                  int64_t N, int64_t K, int32_t layout, int64_t ldo) {
+                  int64_t N, int64_t K, int32_t layout, int64_t ldo, bool b_early = false) {
     if (M <= 0 || N <= 0 || K <= 0) {
         set_error("M, N and K must be positive");
         return 2;
@@ -209,6 +212,7 @@ int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, voi
     c.a = a; c.b = b; c.out = out; c.ldo = ldo;
     c.row_scale = row_scale; c.col_scale = col_scale; c.bias = bias;
     c.M = M; c.N = N; c.K = K;
+    c.b_early = b_early;
     c.a_mn = layout == 2;
     c.b_mn = layout >= 1;
     c.lda = c.a_mn ? M : K;
@@ -415,7 +419,7 @@ int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
     }
     if (int rc = convrot_quantize(as_stream(stream), x, xq, xs, M, K, activation)) return rc;
     return int_mm_common(as_stream(stream), kEpiDequantBf16, xq, w8, out, xs, w_scale, bias, M, N,
-                         K, 0, N);
+                         K, 0, N, true);
 }
 
 int64_t xpuint8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t inner, int32_t activation) {
@@ -451,20 +455,20 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
     if (activation == 4) {
         void *y = ws + L.mid;
         if (int rc = int_mm_common(s, kEpiGegluBf16, xq, up_w8, y, xs, up_scale, nullptr, M, inner,
-                                   K, 0, inner))
+                                   K, 0, inner, true))
             return rc;
         if (int rc = convrot_quantize(s, y, q2, xs2, M, inner, 0)) return rc;
     } else {
         int32_t *acc = reinterpret_cast<int32_t *>(ws + L.mid);
         const int64_t n_up = activation == 5 ? inner : 2 * inner;
         if (int rc = int_mm_common(s, kEpiRawI32, xq, up_w8, acc, nullptr, nullptr, nullptr, M,
-                                   n_up, K, 0, n_up))
+                                   n_up, K, 0, n_up, true))
             return rc;
         if (int rc = dequant_act_quantize(s, acc, q2, xs2, xs, up_scale, M, inner, activation))
             return rc;
     }
     return int_mm_common(s, kEpiDequantBf16, q2, down_w8, out, xs2, down_scale, down_bias, M, K,
-                         inner, 0, K);
+                         inner, 0, K, true);
 }
 
 int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *col_scale,
@@ -592,6 +596,7 @@ int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int
     c.outs = dst; c.nout = nranks; c.ldo = static_cast<int64_t>(nranks) * N;
     c.row_scale = xs; c.col_scale = w_scale; c.bias = bias;
     c.M = M; c.N = N; c.K = K;
+    c.b_early = true;  // the quantizer above is the kernel just before
     return launch_gemm(as_stream(stream), c);
 }
 

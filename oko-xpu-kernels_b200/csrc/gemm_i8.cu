@@ -73,6 +73,8 @@ struct GemmArgs {
     int num_m, num_n, num_k;
     int bn;  // output columns per tile (multiple of 32, 128..256); GEGLU: 128
     // num_m counts 256-row pair tiles
+    int b_early;  // B, the column scales and the bias may be read before the
+                  // wait for the previous kernel (it does not write them)
 };
 
 // The output's tensor maps: one per destination.  Every output tile is
@@ -329,9 +331,11 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // everything above overlaps the previous kernel of the stream; operands,
-    // scales and the output are touched only after it has completed
-    pdl_wait();
+    // Everything above overlaps the previous kernel of the stream.  Each role
+    // waits for that kernel (pdl_wait) before its first global access that may
+    // depend on it: A, the row scales and the output always; B, the column
+    // scales and the bias too unless args.b_early (the linear entries, where
+    // the previous kernel is the activation quantizer).
 
     const int num_tiles = args.num_m * args.num_n;
     constexpr bool GEGLU = (EPI == kEpiGegluBf16);
@@ -349,6 +353,33 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             uint32_t ph = 0;
             uint32_t issued = 0;  // k-blocks issued by this CTA
             const uint32_t pair_tx = static_cast<uint32_t>(2 * (A_BYTES + B_HALF * BK));
+            // this CTA's half of B for k-block kb of output-column block nb into slot st
+            auto load_b = [&](int st, int nb, int kb) {
+                const uint32_t fb = peer_smem(FULL(st), 0);
+                const uint32_t dB = sB + st * B_BYTES;
+                if constexpr (B_MN) {
+                    tma_load_2d_pair(dB, &tmB, fb, nb * BN + static_cast<int>(rank) * 128, kb * BK);
+                } else if constexpr (GEGLU) {
+                    // leader: hidden rows [n, n+128); follower: gate rows [N+n, N+n+128)
+                    tma_load_2d_pair(dB, &tmB, fb, kb * BK, (leader ? 0 : args.N) + nb * 128);
+                } else {
+                    tma_load_2d_pair(dB, &tmB, fb, kb * BK, nb * args.bn + static_cast<int>(rank) * B_HALF);
+                }
+            };
+            // b_early: the B halves of the first pass over the ring load before
+            // the wait (their bytes complete on FULL ahead of the leader's
+            // expect_tx, which the barrier's transaction count allows)
+            uint32_t pre = 0;
+            if (args.b_early) {
+                int tile = pair, kb = 0;
+                for (; pre < static_cast<uint32_t>(STAGES) && tile < num_tiles; ++pre) {
+                    int mb, nb;
+                    tile_coords(tile, args.num_m, args.num_n, mb, nb);
+                    load_b(static_cast<int>(pre), nb, kb);
+                    if (++kb == args.num_k) { kb = 0; tile += npairs; }
+                }
+            }
+            pdl_wait();
             bool ok = true;
             for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 int mb, nb;
@@ -358,17 +389,10 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
                     if (!mbar_wait(EMPTY(stage), ph ^ 1u, fault, 1)) { ok = false; break; }
                     if (leader) mbar_expect_tx(FULL(stage), pair_tx);
                     const uint32_t fb = peer_smem(FULL(stage), 0);
-                    const uint32_t dA = sA + stage * A_BYTES, dB = sB + stage * B_BYTES;
+                    const uint32_t dA = sA + stage * A_BYTES;
                     if constexpr (A_MN) tma_load_2d_pair(dA, &tmA, fb, arow, kb * BK);
                     else tma_load_2d_pair(dA, &tmA, fb, kb * BK, arow);
-                    if constexpr (B_MN) {
-                        tma_load_2d_pair(dB, &tmB, fb, nb * BN + static_cast<int>(rank) * 128, kb * BK);
-                    } else if constexpr (GEGLU) {
-                        // leader: hidden rows [n, n+128); follower: gate rows [N+n, N+n+128)
-                        tma_load_2d_pair(dB, &tmB, fb, kb * BK, (leader ? 0 : args.N) + nb * 128);
-                    } else {
-                        tma_load_2d_pair(dB, &tmB, fb, kb * BK, nb * args.bn + static_cast<int>(rank) * B_HALF);
-                    }
+                    if (issued >= pre) load_b(stage, nb, kb);
                     ++issued;
                     if (++stage == STAGES) { stage = 0; ph ^= 1u; }
                 }
@@ -462,7 +486,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         };
         float pre_w = 1.f, pre_b = 0.f;
         const bool stager = et < 2 * BM;
+        if (!args.b_early) pdl_wait();
         if (stager && pair < num_tiles) fetch(pair, pre_w, pre_b);
+        if (args.b_early) pdl_wait();
         for (int tile = pair; tile < num_tiles; tile += npairs) {
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
@@ -719,6 +745,7 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     a.out = c.out; a.ldo = c.ldo;
     a.row_scale = c.row_scale; a.col_scale = c.col_scale; a.bias = c.bias;
     a.M = static_cast<int>(c.M); a.N = static_cast<int>(c.N); a.K = static_cast<int>(c.K);
+    a.b_early = c.b_early ? 1 : 0;
     a.num_m = static_cast<int>((c.M + 2 * BM - 1) / (2 * BM));
     a.bn = geglu ? 128 : bn;
     a.num_n = static_cast<int>((c.N + a.bn - 1) / a.bn);

@@ -55,6 +55,10 @@ struct GemmCall {
     const float *col_scale = nullptr;  // [N]  (w_scale) or null = 1; GEGLU: [2N]
     const float *bias = nullptr;       // [N]  or null
     int64_t M = 0, N = 0, K = 0;       // GEGLU: N = output width (half of B's rows)
+    // B, col_scale and bias are not written by the kernel launched just before
+    // this GEMM on the stream (the linear entries: that kernel is the
+    // activation quantizer), so the GEMM may load them before waiting for it
+    bool b_early = false;
 };
 int launch_gemm(cudaStream_t s, const GemmCall &c);
 int gemm_fault_status(int reset);  // device fault word of the GEMM waits

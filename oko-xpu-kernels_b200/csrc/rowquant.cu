@@ -33,10 +33,11 @@
 namespace xpuint8 {
 namespace {
 
-// clamp(rint(x / s), +-127) given y = RN(1 / s)
-__device__ __forceinline__ int8_t q_div(float x, float s, float y) {
-    const float r = rintf(div_by_rcp(x, s, y));
-    return static_cast<int8_t>(fmaxf(-127.f, fminf(127.f, r)));
+// the code rint(x / s) given y = RN(1 / s), for |x| <= the maximum s was made
+// from (so |x / s| <= 127 + ulps): the low byte of RN(x / s) + 1.5 * 2^23
+// (round to nearest even by the fp32 add, no conversion instruction)
+__device__ __forceinline__ uint32_t q_div(float x, float s, float y) {
+    return __float_as_uint(__fadd_rn(div_by_rcp(x, s, y), 12582912.0f)) & 0xFFu;
 }
 
 template <bool COLSCALE>
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
         uint2 o;
         uint32_t b[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) b[t] = static_cast<uint8_t>(q_div(v[t], s, y));
+        for (int t = 0; t < 8; ++t) b[t] = q_div(v[t], s, y);
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
         o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
         *reinterpret_cast<uint2 *>(qr + k) = o;
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
     for (int64_t k = kv + threadIdx.x; k < K; k += blockDim.x) {
         float v = bf16_bits_to_f32(xr[k]);
         if constexpr (COLSCALE) v = round_bf16(__fmul_rn(v, round_bf16(cs[k])));
-        qr[k] = q_div(v, s, y);
+        qr[k] = static_cast<int8_t>(q_div(v, s, y));
     }
 }
 
@@ -178,8 +179,7 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
                 uint32_t b[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    // |x / s| <= 127 (+ulps): the magic sum's low byte is rint(x / s)
-                    b[j] = __float_as_uint(__fadd_rn(div_by_rcp(v[8 * c + j], s, y), 12582912.0f)) & 0xFFu;
+                    b[j] = q_div(v[8 * c + j], s, y);
                 }
                 uint2 o;
                 o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict
     const int64_t m1 = min(M, m0 + kColRows);
     float mx[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (n < N) {
-#pragma unroll 4
+#pragma unroll 8
         for (int64_t m = m0 + ty; m < m1; m += 8) {
             const float x = __ldg(xs + m);
             const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
@@ -278,8 +278,8 @@ __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restric
         uint32_t b[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            b[2 * j] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], y[2 * j]));
-            b[2 * j + 1] = static_cast<uint8_t>(q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], y[2 * j + 1]));
+            b[2 * j] = q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], y[2 * j]);
+            b[2 * j + 1] = q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], y[2 * j + 1]);
         }
         uint2 o;
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
