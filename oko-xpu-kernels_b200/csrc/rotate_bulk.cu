@@ -533,8 +533,11 @@ __device__ __forceinline__ void rotate_pair_padded(f2 (&P)[16], uint32_t tile, i
 // one for the quantizer, whose per-batch row-max barrier makes more resident
 // CTAs (8 of 64 registers a thread) worth more than a deeper prefetch
 // (measured at M = 65536, K = 4096: 4.0 TB/s against 3.7-3.9 TB/s).
-__host__ __device__ constexpr int direct_depth(int mode, int) {
-    return mode == 0 ? 1 : 2;
+#ifndef XPUINT8_QUANT_DEPTH
+#define XPUINT8_QUANT_DEPTH 1
+#endif
+__host__ __device__ constexpr int direct_depth(int mode, int act) {
+    return mode == 0 ? ((act == 0 || act == 1 || act == 5) ? XPUINT8_QUANT_DEPTH : 1) : 2;
 }
 // resident 128-thread CTAs per SM the register budget is fitted to: 8 (64
 // registers a thread) at depth 1, XPUINT8_DIRECT_CTAS (96) at depth 2, 4 for
@@ -547,7 +550,8 @@ __host__ __device__ constexpr int direct_depth(int mode, int) {
 #endif
 constexpr int direct_min_ctas128(int mode, int act) {
     return (mode == 0 && act_paired(act)) ? 4
-                                          : (direct_depth(mode, act) == 2 ? XPUINT8_DIRECT_CTAS : XPUINT8_QUANT_CTAS);
+           : mode == 0                    ? XPUINT8_QUANT_CTAS
+                                          : XPUINT8_DIRECT_CTAS;
 }
 
 // SLOTS half-warps per CTA (8 or 16): the row abs-max barrier spans one CTA,
