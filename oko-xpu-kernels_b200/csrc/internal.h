@@ -21,9 +21,10 @@ int num_sms();                        // SM count of the current device
 int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const float *w_scale,
                        const float *x_scale, void *out, float *scale, int64_t M, int64_t K);
 
-// streaming rotation for modes 0, 2, 3 (rotate_bulk.cu); -1 = shape not covered
+// streaming rotation (rotate_bulk.cu); -1 = shape not covered.  row_scale:
+// mode 3's weight scale, mode 1's x_scale; col_scale: mode 1's w_scale
 int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
-                       void *out, float *scale, int64_t M, int64_t K);
+                       const float *col_scale, void *out, float *scale, int64_t M, int64_t K);
 int rot_fault_status(int reset);  // device fault word of the streaming rotation's waits
 // self-check of the quantizers' scale arithmetic (rotate_bulk.cu); counts mismatches
 int check_scale_math(int64_t *bad_scale, int64_t *bad_quant);

@@ -297,9 +297,10 @@ int dispatch_gpl(cudaStream_t s, RotParams p, int gpl, int threads, size_t smem,
 
 int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const float *w_scale,
                        const float *x_scale, void *out, float *scale, int64_t M, int64_t K) {
-    if (mode != 1) {
-        // the streaming kernel (rotate_bulk.cu) covers every shape it fits
-        const int rc = launch_rotate_bulk(s, mode, act, in, w_scale, out, scale, M, K);
+    {
+        // the streaming kernels (rotate_bulk.cu) cover every shape they fit
+        const int rc = mode == 1 ? launch_rotate_bulk(s, 1, act, in, x_scale, w_scale, out, scale, M, K)
+                                 : launch_rotate_bulk(s, mode, act, in, w_scale, nullptr, out, scale, M, K);
         if (rc >= 0) return rc;
     }
     const int64_t G = K / kGroup;

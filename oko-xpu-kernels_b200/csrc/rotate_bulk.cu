@@ -59,7 +59,8 @@ constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
 
 struct BulkParams {
     const uint8_t *in;
-    const float *row_scale;  // mode 3: the weight's per-row scale
+    const float *row_scale;  // mode 3: the weight's per-row scale; mode 1: x_scale [M]
+    const float *col_scale;  // mode 1: the weight scale [K] or [2K]
     uint8_t *out;
     float *scale;            // mode 0: per-row output scale
     int64_t M, K;
@@ -437,60 +438,87 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
 // of a warp on different banks.  A batch's groups are consecutive in the
 // dense output, so each slot writes its pair back with its own bulk copy from
 // its own buffer: the CTA synchronises once per batch, for the row abs-max.
+// Lane l's input of one group: 16 elements, as bf16 (modes 0, 2), int8 (mode
+// 3) or int32 accumulators (mode 1); paired activations also carry the
+// second half (the gate, or SwiGLU's up).
+template <int MODE, int ACT>
+struct GroupIn {
+    static constexpr int kPaired = (MODE <= 1 && act_paired(ACT)) ? 2 : 1;
+    static constexpr int kVec = MODE == 3 ? 1 : (MODE == 1 ? 4 : 2);  // uint4 per half
+    uint4 v[kPaired * kVec];
+};
+template <int MODE, int ACT>
 struct RawPair {
-    uint4 a0, a1, b0, b1;  // lane l's 32 bytes (bf16) or 16 bytes (int8) of each group
-    uint4 c0, c1, d0, d1;  // the second halves of a paired activation
+    GroupIn<MODE, ACT> a, b;  // the slot's two groups
 };
 
 constexpr int kPitch = 144;                 // transpose tile row pitch (128 data + 16 skew)
 constexpr int kTileP = 16 * kPitch;         // 2304 bytes
-__host__ __device__ constexpr int group_out_bytes(int mode) { return mode == 0 ? 256 : 512; }
+__host__ __device__ constexpr int group_out_bytes(int mode) { return mode <= 1 ? 256 : 512; }
 __host__ __device__ constexpr int slot_bytes(int mode) {
     return kTileP + 4 * group_out_bytes(mode) + 32;
 }
 
+// lane l's 16 elements of a group at p (and, paired, at p + half bytes)
 template <int MODE, int ACT>
-__device__ __forceinline__ void load_raw(const uint8_t *pa, bool va, const uint8_t *pb, bool vb,
-                                         uint32_t half, RawPair &r) {
-    if constexpr (MODE == 3) {
-        if (va) r.a0 = __ldcs(reinterpret_cast<const uint4 *>(pa));
-        if (vb) r.b0 = __ldcs(reinterpret_cast<const uint4 *>(pb));
-    } else {
-        if (va) {
-            const uint4 *s = reinterpret_cast<const uint4 *>(pa);
-            r.a0 = __ldcs(s); r.a1 = __ldcs(s + 1);
-            if constexpr (MODE == 0 && act_paired(ACT)) {
-                const uint4 *h = reinterpret_cast<const uint4 *>(pa + half);
-                r.c0 = __ldcs(h); r.c1 = __ldcs(h + 1);
-            }
-        }
-        if (vb) {
-            const uint4 *s = reinterpret_cast<const uint4 *>(pb);
-            r.b0 = __ldcs(s); r.b1 = __ldcs(s + 1);
-            if constexpr (MODE == 0 && act_paired(ACT)) {
-                const uint4 *h = reinterpret_cast<const uint4 *>(pb + half);
-                r.d0 = __ldcs(h); r.d1 = __ldcs(h + 1);
-            }
-        }
+__device__ __forceinline__ void load_group(const uint8_t *p, bool valid, uint32_t half,
+                                           GroupIn<MODE, ACT> &g) {
+    using G = GroupIn<MODE, ACT>;
+    if (!valid) return;
+    const uint4 *s = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+    for (int i = 0; i < G::kVec; ++i) g.v[i] = __ldcs(s + i);
+    if constexpr (G::kPaired == 2) {
+        const uint4 *h = reinterpret_cast<const uint4 *>(p + half);
+#pragma unroll
+        for (int i = 0; i < G::kVec; ++i) g.v[G::kVec + i] = __ldcs(h + i);
     }
 }
 
+// dequant of 4 accumulators: bf16(float(acc) * (w * xs)), the unfused chain's
+// rounding (src/xpuint8.cpp:246-248)
+__device__ __forceinline__ void dequant4(const uint4 &a, const float4 &w, float xs, float *h) {
+    h[0] = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(a.x)), __fmul_rn(w.x, xs)));
+    h[1] = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(a.y)), __fmul_rn(w.y, xs)));
+    h[2] = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(a.z)), __fmul_rn(w.z, xs)));
+    h[3] = round_bf16(__fmul_rn(static_cast<float>(static_cast<int32_t>(a.w)), __fmul_rn(w.w, xs)));
+}
+
+// The 16 fp32 values lane l feeds the rotation.  s: mode 3's row scale, mode
+// 1's x_scale; ws: mode 1's weight scales of the group's 16 (hidden) columns,
+// ws + K those of the gate columns.
 template <int MODE, int ACT>
-__device__ __forceinline__ void decode(const uint4 &x0, const uint4 &x1, const uint4 &y0,
-                                       const uint4 &y1, float s, float (&v)[16]) {
+__device__ __forceinline__ void decode(const GroupIn<MODE, ACT> &g, float s, const float *ws,
+                                       int64_t K, float (&v)[16]) {
     if constexpr (MODE == 3) {
-        const uint32_t w[4] = {x0.x, x0.y, x0.z, x0.w};
+        const uint32_t w[4] = {g.v[0].x, g.v[0].y, g.v[0].z, g.v[0].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int t = 0; t < 4; ++t)
                 v[4 * j + t] = round_bf16(
                     __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * t)) & 0xFF)), s));
+    } else if constexpr (MODE == 1) {
+        const float4 *wh = reinterpret_cast<const float4 *>(ws);
+        float h[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dequant4(g.v[j], __ldg(wh + j), s, h + 4 * j);
+        if constexpr (act_paired(ACT)) {
+            const float4 *wg = reinterpret_cast<const float4 *>(ws + K);
+            float q[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dequant4(g.v[4 + j], __ldg(wg + j), s, q + 4 * j);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(h[t], q[t]);
+        } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(h[t], 0.f);
+        }
     } else {
-        unpack16_bf16(x0, x1, v);
+        unpack16_bf16(g.v[0], g.v[1], v);
         if constexpr (MODE == 0 && act_paired(ACT)) {
             float u[16];
-            unpack16_bf16(y0, y1, u);
+            unpack16_bf16(g.v[2], g.v[3], u);
 #pragma unroll
             for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], u[t]);
         } else if constexpr (MODE == 0 && ACT != 0) {
@@ -537,11 +565,12 @@ __device__ __forceinline__ void rotate_pair_padded(f2 (&P)[16], uint32_t tile, i
 #define XPUINT8_QUANT_DEPTH 1
 #endif
 __host__ __device__ constexpr int direct_depth(int mode, int act) {
-    return mode == 0 ? ((act == 0 || act == 1 || act == 5) ? XPUINT8_QUANT_DEPTH : 1) : 2;
+    return mode == 1 ? 1 : (mode == 0 ? ((act == 0 || act == 1 || act == 5) ? XPUINT8_QUANT_DEPTH : 1) : 2);
 }
-// resident 128-thread CTAs per SM the register budget is fitted to: 8 (64
-// registers a thread) at depth 1, XPUINT8_DIRECT_CTAS (96) at depth 2, 4 for
-// the paired activations
+// resident 128-thread CTAs per SM the register budget is fitted to:
+// XPUINT8_QUANT_CTAS (72 registers a thread) for the quantizer,
+// XPUINT8_DIRECT_CTAS (96) for the two-deep rotations, 4 (128) for paired
+// inputs and for mode 1's int32 accumulators (64 registers of loads in flight)
 #ifndef XPUINT8_DIRECT_CTAS
 #define XPUINT8_DIRECT_CTAS 5
 #endif
@@ -549,20 +578,22 @@ __host__ __device__ constexpr int direct_depth(int mode, int act) {
 #define XPUINT8_QUANT_CTAS 7
 #endif
 constexpr int direct_min_ctas128(int mode, int act) {
-    return (mode == 0 && act_paired(act)) ? 4
-           : mode == 0                    ? XPUINT8_QUANT_CTAS
-                                          : XPUINT8_DIRECT_CTAS;
+    return ((mode == 0 && act_paired(act)) || mode == 1) ? 4
+           : mode == 0                                   ? XPUINT8_QUANT_CTAS
+                                                         : XPUINT8_DIRECT_CTAS;
 }
 
-// SLOTS half-warps per CTA (8 or 16): the row abs-max barrier spans one CTA,
-// so the smaller CTA keeps it to the warps of one row at K <= 4096
+// SLOTS half-warps per CTA (8, 10, 12 or 16): a batch is the R rows whose
+// groups fill the slots (R * G <= 2 * SLOTS), so the row abs-max barrier spans
+// one CTA of the size the row width suits (K = 1280: 10 slots, 4 rows;
+// K = 4096: 8 slots, one row; K = 5120: 10 slots, one row)
 template <int MODE, int ACT, int SLOTS>
 __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 / SLOTS)
     rotate_direct_kernel(const BulkParams p) {
     constexpr int DEPTH = direct_depth(MODE, ACT);
-    constexpr bool QUANT = (MODE == 0);
+    constexpr bool QUANT = (MODE <= 1);
     constexpr int GOB = group_out_bytes(MODE);  // output bytes of one group
-    constexpr int IEB = (MODE == 3) ? 1 : 2;    // input bytes per element
+    constexpr int IEB = MODE == 3 ? 1 : (MODE == 1 ? 4 : 2);  // input bytes per element
     extern __shared__ __align__(128) uint8_t smem[];
     const int slot = threadIdx.x >> 4, l = threadIdx.x & 15;
     const uint32_t tile = smem_u32(smem) + slot * slot_bytes(MODE);
@@ -578,7 +609,11 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
     // byte offsets inside a batch (a batch is at most 32 rows of at most 32 KB)
     const uint32_t off0 = r0 * p.in_row_bytes + (g0 * 256 + l * 16) * IEB;
     const uint32_t off1 = r1 * p.in_row_bytes + (g1 * 256 + l * 16) * IEB;
-    const uint32_t half = 2 * static_cast<uint32_t>(p.K);  // a paired activation's second half
+    // a paired input's second half, in bytes
+    const uint32_t half = static_cast<uint32_t>(IEB) * static_cast<uint32_t>(p.K);
+    // mode 1: the weight scales of each group's columns
+    const float *ws0 = MODE == 1 ? p.col_scale + g0 * 256 + l * 16 : nullptr;
+    const float *ws1 = MODE == 1 ? p.col_scale + g1 * 256 + l * 16 : nullptr;
 
     if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
     __syncthreads();
@@ -593,16 +628,17 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
         return static_cast<int>(left < p.R ? left : p.R);
     };
     // load batch b (when it exists) into r
-    auto fetch = [&](int b, RawPair &r) {
+    auto fetch = [&](int b, RawPair<MODE, ACT> &r) {
         if (b < p.nbatch) {
             const int rows = batch_rows(b);
             const uint8_t *src = p.in + static_cast<int64_t>(b) * p.R * p.in_row_bytes;
-            load_raw<MODE, ACT>(src + off0, in0 && r0 < rows, src + off1, in1 && r1 < rows, half, r);
+            load_group<MODE, ACT>(src + off0, in0 && r0 < rows, half, r.a);
+            load_group<MODE, ACT>(src + off1, in1 && r1 < rows, half, r.b);
         }
     };
     // transform batch b (k-th of this CTA) from raw, whose registers then take
     // the load of batch b + DEPTH * gridDim.x
-    auto batch = [&](int b, int k, RawPair &raw) {
+    auto batch = [&](int b, int k, RawPair<MODE, ACT> &raw) {
         const int rows = batch_rows(b);
         const int64_t row0 = static_cast<int64_t>(b) * p.R;
         const bool v0 = in0 && r0 < rows, v1 = in1 && r1 < rows;
@@ -610,13 +646,15 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
 
         float a[16], c[16];
         if (v0) {
-            decode<MODE, ACT>(raw.a0, raw.a1, raw.c0, raw.c1, MODE == 3 ? __ldg(p.row_scale + row0 + r0) : 0.f, a);
+            decode<MODE, ACT>(raw.a, MODE == 3 || MODE == 1 ? __ldg(p.row_scale + row0 + r0) : 0.f, ws0,
+                              p.K, a);
         } else {
 #pragma unroll
             for (int t = 0; t < 16; ++t) a[t] = 0.f;
         }
         if (v1) {
-            decode<MODE, ACT>(raw.b0, raw.b1, raw.d0, raw.d1, MODE == 3 ? __ldg(p.row_scale + row0 + r1) : 0.f, c);
+            decode<MODE, ACT>(raw.b, MODE == 3 || MODE == 1 ? __ldg(p.row_scale + row0 + r1) : 0.f, ws1,
+                              p.K, c);
         } else {
 #pragma unroll
             for (int t = 0; t < 16; ++t) c[t] = 0.f;
@@ -705,7 +743,7 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
             bulk_commit();
         }
     };
-    RawPair ra{}, rb{};
+    RawPair<MODE, ACT> ra{}, rb{};
     fetch(blockIdx.x, ra);
     if constexpr (DEPTH == 2) fetch(blockIdx.x + gridDim.x, rb);
     int k = 0;
@@ -754,7 +792,12 @@ int launch_direct(cudaStream_t s, const BulkParams &p) {
 }
 template <int MODE, int ACT>
 int launch_direct(cudaStream_t s, const BulkParams &p, int slots) {
-    return slots == 8 ? launch_direct<MODE, ACT, 8>(s, p) : launch_direct<MODE, ACT, 16>(s, p);
+    switch (slots) {
+        case 8: return launch_direct<MODE, ACT, 8>(s, p);
+        case 10: return launch_direct<MODE, ACT, 10>(s, p);
+        case 12: return launch_direct<MODE, ACT, 12>(s, p);
+        default: return launch_direct<MODE, ACT, 16>(s, p);
+    }
 }
 
 template <int MODE, int ACT>
@@ -793,7 +836,7 @@ int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
 // Returns -1 when the shape does not fit the streaming kernel (the caller then
 // uses the register-staged kernel of rotate.cu).
 int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
-                       void *out, float *scale, int64_t M, int64_t K) {
+                       const float *col_scale, void *out, float *scale, int64_t M, int64_t K) {
     const int64_t G = K / kGroup;
     int pps = 0, R = 0;
     double best = -1;
@@ -804,17 +847,20 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
         if (util >= 0.85) { pps = c; R = r; break; }
         if (util > best) { best = util; pps = c; R = r; }
     }
-    if (pps == 0 || R < 1) return -1;
+    if (!(kDirect && G <= 32) && (pps == 0 || R < 1)) return -1;
     if (R > 32) R = 32;
+    if (R < 1) R = 1;
     BulkParams p{};
     p.in = static_cast<const uint8_t *>(in);
     p.row_scale = row_scale;
+    p.col_scale = col_scale;
     p.out = static_cast<uint8_t *>(out);
     p.scale = scale;
     p.M = M; p.K = K; p.G = static_cast<int>(G); p.R = R;
-    const bool paired = mode == 0 && act_paired(act);
-    p.in_row_bytes = static_cast<uint32_t>(mode == 3 ? K : (paired ? 4 * K : 2 * K));
-    p.out_row_bytes = static_cast<uint32_t>(mode == 0 ? K : 2 * K);
+    const bool paired = mode <= 1 && act_paired(act);
+    const int64_t in_elem = mode == 3 ? 1 : (mode == 1 ? 4 : 2);
+    p.in_row_bytes = static_cast<uint32_t>(in_elem * K * (paired ? 2 : 1));
+    p.out_row_bytes = static_cast<uint32_t>(mode <= 1 ? K : 2 * K);
     auto up = [](uint32_t x) { return (x + 127u) & ~127u; };
     p.in_stage_bytes = up(R * p.in_row_bytes);
     p.out_stage_bytes = up(R * p.out_row_bytes);
@@ -847,13 +893,21 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     }
     if (best_ctas == 0) return -1;
     const size_t smem = total(p.ns, p.os);
-    if (kDirect && pps == 1) {
-        // one batch per CTA-sized team of half-warps: 8 slots (128 threads)
-        // when a row has at most 16 groups, else 16
-        int slots = G <= 16 ? 8 : 16;
-        // XPUINT8_ROTATE_SLOTS=16 keeps 256-thread CTAs for every shape (tuning)
+    if (kDirect && G <= 32) {
+        // one batch per CTA-sized team of half-warps: the team size whose
+        // batches fill the most slots, the smallest of equals
+        int slots = 16;
+        double best_fill = -1.0;
+        for (int c : {8, 10, 12, 16}) {
+            if (G > 2 * c) continue;
+            const int64_t r = std::min<int64_t>(32, (2 * c) / G);
+            const double fill = static_cast<double>(r * G) / (2 * c);
+            if (fill > best_fill + 1e-9) { best_fill = fill; slots = c; }
+        }
+        // XPUINT8_ROTATE_SLOTS=8|10|12|16 fixes the team size (tuning)
         if (const char *f = std::getenv("XPUINT8_ROTATE_SLOTS")) {
-            if (std::atoi(f) == 16) slots = 16;
+            const int v = std::atoi(f);
+            if ((v == 8 || v == 10 || v == 12 || v == 16) && G <= 2 * v) slots = v;
         }
         p.R = static_cast<int>(std::min<int64_t>(32, (2 * slots) / G));
         const int64_t nbd = (M + p.R - 1) / p.R;
@@ -867,6 +921,14 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
                 case 3: return launch_direct<0, 3>(s, p, slots);
                 case 4: return launch_direct<0, 4>(s, p, slots);
                 case 5: return launch_direct<0, 5>(s, p, slots);
+                default: return -1;
+            }
+        }
+        if (mode == 1) {
+            switch (act) {
+                case 3: return launch_direct<1, 3>(s, p, slots);
+                case 4: return launch_direct<1, 4>(s, p, slots);
+                case 5: return launch_direct<1, 5>(s, p, slots);
                 default: return -1;
             }
         }
