@@ -591,7 +591,8 @@ int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int
     }
     if (int rc = convrot_quantize(as_stream(stream), x, xq, xs, M, K, activation)) return rc;
     GemmCall c;
-    c.epilogue = kEpiDequantBf16;
+    // 128-byte row segments per store: the tiles cross NVLink in larger writes
+    c.epilogue = kEpiDequantWide;
     c.a = xq; c.b = w8; c.lda = K; c.ldb = K;
     c.outs = dst; c.nout = nranks; c.ldo = static_cast<int64_t>(nranks) * N;
     c.row_scale = xs; c.col_scale = w_scale; c.bias = bias;

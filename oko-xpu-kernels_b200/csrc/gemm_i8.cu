@@ -114,8 +114,11 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 // rows (bf16; int32 uses 16-column chunks) is converted in registers, written
 // to one buffer and handed to a TMA bulk-tensor store, which also clips the
 // M/N tails; the next buffers are filled meanwhile.
-constexpr int kStageBytes = 32 * 64;
 constexpr int kStageBufs = 2;                                  // per epilogue warp
+// a staging buffer: 32 rows of 64 bytes, or of 128 bytes (128-byte swizzle:
+// chunk c of row r at c ^ (r & 7)) for the wide-store epilogue
+template <int EPI>
+constexpr int stage_bytes() { return EPI == kEpiDequantWide ? 32 * 128 : 32 * 64; }
 
 // Per-epilogue configuration.  The epilogue warps come in groups of four, one
 // per TMEM lane quarter (warp w reads lanes 32*(w%4)..+31), each group draining
@@ -128,8 +131,8 @@ struct Cfg {
     static constexpr int kEpiWarps = 8;
     static constexpr int kGroups = kEpiWarps / 4;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
-    static constexpr int kStages = 6;
-    static constexpr int kEpiSmem = kEpiWarps * kStageBufs * kStageBytes;
+    static constexpr int kStages = EPI == kEpiDequantWide ? 5 : 6;
+    static constexpr int kEpiSmem = kEpiWarps * kStageBufs * stage_bytes<EPI>();
     static constexpr size_t kSmemBytes =
         static_cast<size_t>(kStages) * STAGE_BYTES + kEpiSmem + 2 * BN * 4 + 256;
     static_assert(kSmemBytes <= 232448, "over the 227 KB shared-memory limit of a CTA");
@@ -137,6 +140,17 @@ struct Cfg {
 
 __device__ __forceinline__ uint32_t stage_chunk_addr(uint32_t buf, int row, int c) {
     return buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4);
+}
+__device__ __forceinline__ uint32_t stage_chunk_addr_wide(uint32_t buf, int row, int c) {
+    return buf + row * 128 + ((c ^ (row & 7)) << 4);
+}
+// 32 bf16 results of this row into half h (columns 32h..32h+31) of a wide buffer
+__device__ __forceinline__ void stage_bf16_32_wide(uint32_t buf, int lane, int h, const float (&v)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        st_shared_v4(stage_chunk_addr_wide(buf, lane, 4 * h + c), cvt_bf16x2(v[8 * c], v[8 * c + 1]),
+                     cvt_bf16x2(v[8 * c + 2], v[8 * c + 3]), cvt_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                     cvt_bf16x2(v[8 * c + 6], v[8 * c + 7]));
 }
 
 // one 32-column chunk of bf16 output: v[0..31] are the fp32 results of this row
@@ -231,6 +245,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
     const int y = m0 + quarter * 32;
     const f2 xs2 = mk2(xs, xs);
     const bool bias = a.bias != nullptr;
+    constexpr int kStageBytes = stage_bytes<EPI>();
+    if constexpr (EPI == kEpiDequantWide) {
+        // 64 columns per store (the tile width is a multiple of 64)
+#pragma unroll 1
+        for (int c = c0; c < c1; c += 64) {
+            if (n0 + c >= a.N) break;
+            uint32_t r0[32], r1[32];
+            tmem_ld32(taddr + c, r0);
+            tmem_ld32(taddr + c + 32, r1);
+            stage_reserve(lane);
+            const uint32_t buf = bufs + bsel * kStageBytes;
+            float v[32];
+            tmem_wait_ld(r0);
+            dequant32(r0, s_ws + c, s_b + c, xs2, bias, v);
+            stage_bf16_32_wide(buf, lane, 0, v);
+            tmem_wait_ld(r1);
+            dequant32(r1, s_ws + c + 32, s_b + c + 32, xs2, bias, v);
+            stage_bf16_32_wide(buf, lane, 1, v);
+            stage_flush(tmOut, buf, lane, n0 + c, y);
+            bsel ^= 1;
+        }
+        return;
+    }
 #pragma unroll 1
     for (int c = c0; c < c1; c += 32) {
         if (n0 + c >= a.N) break;
@@ -459,7 +496,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         const int col1 = GEGLU ? col0 + kCols : min(col0 + kCols, args.bn);
         const int et = threadIdx.x - 64;      // index among the epilogue threads; the
                                               // first 256 stage the tile's column scales
-        const uint32_t bufs = sEpi + (warp - 2) * kStageBufs * kStageBytes;
+        const uint32_t bufs = sEpi + (warp - 2) * kStageBufs * stage_bytes<EPI>();
         const uint32_t tempty_leader0 = peer_smem(TEMPTY(0), 0);
         int bsel = 0;
         int acc = 0;
@@ -684,16 +721,18 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     // fixed drain and hand-over, counted as 32 columns.  Only a K-major B is
     // narrowed: an MN-major B tile is loaded as two 128-column boxes.
     int bn = BN;
+    const bool wide = c.epilogue == kEpiDequantWide;
+    const int step = wide ? 64 : 32;  // the wide epilogue stores 64 columns at a time
     // XPUINT8_GEMM_BN=<128..256, multiple of 32> fixes the width (tests, tuning)
     const char *force = std::getenv("XPUINT8_GEMM_BN");
     const int forced = force ? std::atoi(force) : 0;
-    if (!geglu && !c.b_mn && forced >= 128 && forced <= BN && forced % 32 == 0) {
+    if (!geglu && !c.b_mn && forced >= 128 && forced <= BN && forced % step == 0) {
         bn = forced;
     } else if (!geglu && !c.b_mn) {
         const int64_t sms = num_sms() / 2;  // CTA pairs
         const int64_t num_m = (c.M + 2 * BM - 1) / (2 * BM);
         int64_t best = -1;
-        for (int cand = BN; cand >= 128; cand -= 32) {
+        for (int cand = BN; cand >= 128; cand -= step) {
             const int64_t tiles = num_m * ((c.N + cand - 1) / cand);
             const int64_t cost = ((tiles + sms - 1) / sms) * (cand + 32);
             if (best < 0 || cost < best) {
@@ -735,6 +774,10 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
             if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_INT32,
                           CU_TENSOR_MAP_SWIZZLE_64B))
                 return 2;
+        } else if (wide) {
+            if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 2, 64, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+                return 2;
         } else {
             if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                           CU_TENSOR_MAP_SWIZZLE_64B))
@@ -768,6 +811,9 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
             break;
         case kEpiGegluBf16:
             return launch_sized<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, tiles);
+        case kEpiDequantWide:
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantWide, false, false>(s, ma, mb, mo, a, tiles);
+            break;
         default:
             break;
     }

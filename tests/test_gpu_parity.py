@@ -356,6 +356,38 @@ def test_linear_matches_the_oracle(m, n, k):
     assert np.array_equal(got, ref)
 
 
+@pytest.mark.parametrize("m,n_local,k", [(1000, 1040, 1280), (256, 64, 256), (77, 1792, 4096)])
+def test_allgather_epilogue_on_one_gpu(m, n_local, k):
+    """The all-gather linear's multi-destination, wide-store epilogue on one GPU:
+    two 'ranks' (two calls with rank 0 and 1 and their own weight blocks) store
+    their column blocks into two local buffers; both buffers must equal the
+    linear of the whole weight, bit for bit."""
+    import ctypes
+    from xpu_kernels import int8
+    from xpu_kernels.int8 import _lib as L
+    lib = L.load()
+    n = 2 * n_local
+    _, w8n, wsn = _prep(n, k, 180 + k)
+    w8, ws = torch.from_numpy(w8n).to(DEV), torch.from_numpy(wsn).to(DEV)
+    x = rand_bf16((m, k), 181 + m, outliers=4).to(DEV)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(n)) * 0.01).to(DEV)
+    full = int8.linear(x, w8, ws, bias)
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(2)]
+    table = (ctypes.c_void_p * 2)(*[o.data_ptr() for o in outs])
+    xq = torch.empty(m, k, dtype=torch.int8, device=DEV)
+    xs = torch.empty(m, dtype=torch.float32, device=DEV)
+    for r in range(2):
+        sl = slice(r * n_local, (r + 1) * n_local)
+        w8r, wsr, br = w8[sl].contiguous(), ws[sl].contiguous(), bias[sl].contiguous()
+        rc = lib.xpuint8_linear_allgather_stream(L._stream(torch.device(DEV)), L._ptr(x), L._ptr(w8r),
+                                                 L._ptr(wsr), L._ptr(br), table, 2, r, L._ptr(xq),
+                                                 L._ptr(xs), m, n_local, k, 0)
+        assert rc == 0, lib.xpuint8_last_error()
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o.view(torch.int16), full.view(torch.int16))
+
+
 def test_prepare_weight_matches_the_reference_fixture():
     from xpu_kernels import int8
     import os
