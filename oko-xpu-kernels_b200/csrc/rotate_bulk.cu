@@ -628,12 +628,15 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
         return static_cast<int>(left < p.R ? left : p.R);
     };
     // load batch b (when it exists) into r
+    // (an invalid group -- a row past the end of a partial last batch, or the
+    // odd slot of an odd group count -- loads the batch's first bytes, which
+    // are in bounds: no branch around the loads or the decode)
     auto fetch = [&](int b, RawPair<MODE, ACT> &r) {
         if (b < p.nbatch) {
             const int rows = batch_rows(b);
             const uint8_t *src = p.in + static_cast<int64_t>(b) * p.R * p.in_row_bytes;
-            load_group<MODE, ACT>(src + off0, in0 && r0 < rows, half, r.a);
-            load_group<MODE, ACT>(src + off1, in1 && r1 < rows, half, r.b);
+            load_group<MODE, ACT>((in0 && r0 < rows) ? src + off0 : src, true, half, r.a);
+            load_group<MODE, ACT>((in1 && r1 < rows) ? src + off1 : src, true, half, r.b);
         }
     };
     // transform batch b (k-th of this CTA) from raw, whose registers then take
@@ -644,21 +647,13 @@ __global__ void __launch_bounds__(SLOTS * 16, direct_min_ctas128(MODE, ACT) * 8 
         const bool v0 = in0 && r0 < rows, v1 = in1 && r1 < rows;
         unsigned int *amax_now = row_amax + 32 * (k % 3);
 
+        // An invalid group's values stay in its own half of the packed
+        // arithmetic: it posts no maximum, no scale and no stored byte.
         float a[16], c[16];
-        if (v0) {
-            decode<MODE, ACT>(raw.a, MODE == 3 || MODE == 1 ? __ldg(p.row_scale + row0 + r0) : 0.f, ws0,
-                              p.K, a);
-        } else {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) a[t] = 0.f;
-        }
-        if (v1) {
-            decode<MODE, ACT>(raw.b, MODE == 3 || MODE == 1 ? __ldg(p.row_scale + row0 + r1) : 0.f, ws1,
-                              p.K, c);
-        } else {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) c[t] = 0.f;
-        }
+        const float s0 = (MODE == 3 || MODE == 1) ? __ldg(p.row_scale + row0 + (v0 ? r0 : 0)) : 0.f;
+        const float s1 = (MODE == 3 || MODE == 1) ? __ldg(p.row_scale + row0 + (v1 ? r1 : 0)) : 0.f;
+        decode<MODE, ACT>(raw.a, s0, ws0, p.K, a);
+        decode<MODE, ACT>(raw.b, s1, ws1, p.K, c);
         // the loads of DEPTH batches on fly while this one is transformed
         fetch(b + DEPTH * static_cast<int>(gridDim.x), raw);
         f2 vals[16];
