@@ -266,8 +266,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             stage_flush(tmOut, buf, lane, n0 + c, y);
             bsel ^= 1;
         }
-        return;
-    }
+    } else {
 #pragma unroll 1
     for (int c = c0; c < c1; c += 32) {
         if (n0 + c >= a.N) break;
@@ -304,6 +303,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             stage_flush(tmOut, buf, lane, n0 + c, y);
             bsel ^= 1;
         }
+    }
     }
 }
 
