@@ -1,10 +1,10 @@
-"""The sharded INT8 linear on two GPUs, bit for bit against one GPU.
+"""The sharded INT8 linear on every visible GPU (2 to 8), bit for bit against one GPU.
 
 Rows are independent, so the M-sharded result of each rank must equal the
 single-GPU result on those rows exactly; the N-sharded all-gather (NCCL, and
 the GEMM whose epilogue stores into the peers' buffers over NVLink) must
-rebuild the single-GPU output exactly.  Skipped when fewer than two GPUs are
-visible.  NVLS is off (NCCL_NVLS_ENABLE=0) and the fused path uses plain peer
+rebuild the single-GPU output exactly.  The tests use every visible GPU, up
+to 8 ranks, and are skipped when fewer than two are visible.  NVLS is off (NCCL_NVLS_ENABLE=0) and the fused path uses plain peer
 stores, no multicast.
 """
 
@@ -61,10 +61,15 @@ def _worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_sharded_linear_on_two_gpus(tmp_path):
-    if torch.cuda.device_count() < 2:
+def _world():
+    n = min(torch.cuda.device_count(), 8)
+    if n < 2:
         pytest.skip("needs two GPUs")
-    world = 2
+    return n
+
+
+def test_sharded_linear_on_all_gpus(tmp_path):
+    world = _world()
     ctx = mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                              join=False, start_method="spawn")
     while not ctx.join(timeout=300):
@@ -109,10 +114,8 @@ def _fused_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_fused_allgather_linear_on_two_gpus(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+def test_fused_allgather_linear_on_all_gpus(tmp_path):
+    world = _world()
     ctx = mp.start_processes(_fused_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                              join=False, start_method="spawn")
     while not ctx.join(timeout=300):
