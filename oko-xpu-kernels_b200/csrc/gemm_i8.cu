@@ -44,6 +44,7 @@
 // MMAs (again with a bound), frees its TMEM and returns.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -621,8 +622,12 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
 // CTA pairs that can be resident at once for this kernel (cached per device)
 template <int EPI, bool A_MN, bool B_MN>
 int resident_pairs(int dev) {
-    static int cached[32] = {0};
-    if (dev < 32 && cached[dev] > 0) return cached[dev];
+    // atomic: first calls from several host threads may race to fill it (same value)
+    static std::atomic<int> cached[32] = {};
+    if (dev >= 0 && dev < 32) {
+        const int c = cached[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
     auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
@@ -640,7 +645,7 @@ int resident_pairs(int dev) {
     cfg.numAttrs = 1;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) return -1;
-    if (dev < 32) cached[dev] = n;
+    if (dev >= 0 && dev < 32) cached[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 

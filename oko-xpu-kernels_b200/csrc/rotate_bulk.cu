@@ -32,7 +32,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -764,14 +766,18 @@ int launch_direct(cudaStream_t s, const BulkParams &p) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return launch_status("rotate (shared memory attribute)");
-    static int cached_per_sm = 0;
-    if (cached_per_sm == 0) {
+    // resident CTAs per SM (atomic: first calls from several host threads may
+    // race to fill it, with the same value)
+    static std::atomic<int> cached_per_sm{0};
+    int per_sm = cached_per_sm.load(std::memory_order_relaxed);
+    if (per_sm == 0) {
         int per = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, SLOTS * 16, smem) != cudaSuccess)
             per = 1;
-        cached_per_sm = std::max(1, per);
+        per_sm = std::max(1, per);
+        cached_per_sm.store(per_sm, std::memory_order_relaxed);
     }
-    const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * cached_per_sm);
+    const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * per_sm);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -801,17 +807,23 @@ int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)) != cudaSuccess)
             return launch_status("rotate (shared memory attribute)");
-        // resident blocks per SM for this kernel and shared-memory size (cached)
+        // resident blocks per SM for this kernel and shared-memory size (cached;
+        // the pair is read and updated under a lock)
+        static std::mutex cache_mu;
         static size_t cached_smem = 0;
         static int cached_per_sm = 0;
-        if (cached_smem != smem) {
-            int per = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess)
-                per = 1;
-            cached_per_sm = std::max(1, per);
-            cached_smem = smem;
+        int per_sm;
+        {
+            std::lock_guard<std::mutex> lock(cache_mu);
+            if (cached_smem != smem) {
+                int per = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess)
+                    per = 1;
+                cached_per_sm = std::max(1, per);
+                cached_smem = smem;
+            }
+            per_sm = cached_per_sm;
         }
-        const int per_sm = cached_per_sm;
         const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * per_sm);
         kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
         return launch_status("rotate");
