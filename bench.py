@@ -5,32 +5,41 @@ rotate+quant HBM GB/s".  One step is one INT8 ConvRot linear forward over one
 batch: rotate+quantize bf16 x [2048,1280] -> int8, then the tcgen05 int8 GEMM
 against the pre-rotated int8 weight [10240,1280] with the dequant epilogue
 fused -> bf16 [2048,10240] (the SDXL GEGLU up-projection shape, config C3/W1).
-``value`` = 2*M*N*K ops per step x steps x ranks / the device time of the
-timed region (max over ranks), in TOPS; inputs resident in HBM, six rotating
-buffer sets (x, weight, scales, output: 378 MB in all, three times the 126 MB
-L2) so no step reads the L2-resident leftovers of the previous one.  The
-timed steps are replayed from CUDA graphs of the same launches.
+
+Timing: the K = --steps steps of a timed region are replayed from CUDA graphs
+of exactly those launches (a graph of min(K, 600) steps, replayed, plus a graph
+of the remainder); the region is repeated R times back to back on the stream,
+each repetition timed by its own CUDA events, R chosen so the repetitions
+cover about 2.5 s (the clock sampler's window); ``ms_per_step`` is the median
+repetition / K, max over ranks.  ``value`` = 2*M*N*K ops x ranks / that time,
+in TOPS; inputs resident in HBM, six rotating buffer sets (x, weight, scales,
+output: 378 MB in all, three times the 126 MB L2) so no step reads the
+L2-resident leftovers of the previous one.
 
 Also reported on the same line:
 * ``roofline``: the GEMM kernel alone (its average launch time by CUDA
   events), achieved int8 TOPS against the int8 dense peak (2x the measured
-  bf16 cuBLAS burst of MEASURED_PEAKS.json), with the DRAM traffic of one
-  launch from the committed ncu summary;
+  bf16 cuBLAS burst of MEASURED_PEAKS.json) and against cuBLASLt's int8 GEMM
+  measured here at 8192^3, with the DRAM traffic of one launch from the
+  committed ncu summary;
 * ``rotate_quant``: the rotate+quantize kernel at config C5 (x [65536,4096],
   3*M*K + 4*M = 805.6 MB per launch) in HBM GB/s against the measured copy
   bandwidth -- the metric's second half;
+* ``c5_mshard``: config C5 (x [65536,4096]) M-sharded over the ranks with the
+  [4096,4096] and [14336,4096] weights replicated: whole-job TOPS, strong
+  scaling (no collective on the data path);
+* ``c5_nshard`` (N > 1): config C5's N-sharded variant, the [14336,4096]
+  weight split by output channels with the output all-gather fused into the
+  GEMM epilogue (peer stores over NVLink), and the NCCL form;
 * ``e2e``: the same step through the public API ``xpu_kernels.linear`` with x
   copied from pinned host memory and the bf16 result copied back each step;
-* ``cpu_baseline``: the CPU oracle (the reference path restated in numpy,
-  float64 BLAS for the exact int8 GEMM) on a row sample of the workload.
+* ``cpu_baseline``: the reference's own CPU path (reference/convrot_linear.py's
+  op sequence with torch._int_mm, the Hadamard in place of its identity
+  placeholder), restated in oracle/convrot_torch_cpu.py, on the full workload.
 
-``--impl reference`` times the reference's CPU path (the oracle port: the
-reference's own library is SYCL for Intel GPUs and does not build here) on
-the host cores, on the same metric and unit.
-
-Multi-GPU (torchrun): every rank runs its own 2048-row batch against a
-replicated weight (M-sharding, no collective on the data path): "scaling":
-"weak".
+``--impl reference`` times that same CPU path on the host cores (the
+reference's device library is SYCL for Intel GPUs and does not build here) on
+the same metric, unit and workload.
 """
 
 from __future__ import annotations
@@ -146,22 +155,58 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- CPU arms
 
+REF_SAMPLE = ("the reference's CPU path: reference/convrot_linear.py:5-23's op sequence "
+              "(bf16 group matmul with the Hadamard, row abs-max scale, round/clamp, "
+              "torch._int_mm against the transposed int8 weight, bf16 dequant), restated in "
+              "torch in oracle/convrot_torch_cpu.py, on the full M=2048 x K=1280 x N=10240 "
+              "workload per step")
+
+
 def _cpu_inputs(rows, seed=2):
     g = torch.Generator().manual_seed(seed)
-    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
+    x = torch.randn(rows, K, generator=g)
+    x[:, :13] *= 10
+    x = x.to(torch.bfloat16)
     w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
-    xb = x.view(torch.int16).numpy().view(np.uint16)
-    wb = w.view(torch.int16).numpy().view(np.uint16)
-    return xb, wb
+    bias = (torch.randn(N, generator=g) * 0.01).to(torch.bfloat16)
+    return x, w, bias
 
 
-def cpu_oracle_rate(rows: int, budget_s: float):
-    """TOPS of the CPU oracle's forward on `rows` rows of the workload, repeated
-    for about `budget_s` seconds (the weight is prepared once, untimed)."""
+def _cpu_reference_setup():
+    """The workload for the reference's CPU path: x, the prepared int8 weight
+    (prepare_weight's format, made by the numpy oracle once, untimed)."""
     from oracle import convrot_oracle as O
-    xb, wb = _cpu_inputs(rows)
-    w8, ws = O.prepare_weight(wb)
-    O.linear(xb[:8], w8, ws)  # warm the BLAS threads
+    from oracle import convrot_torch_cpu as T
+    x, w, bias = _cpu_inputs(M)
+    w8, ws = O.prepare_weight(w.view(torch.int16).numpy().view(np.uint16))
+    return x, torch.from_numpy(w8), torch.from_numpy(ws), bias, T.hadamard_bf16(), T
+
+
+def cpu_reference_rate(budget_s: float):
+    """TOPS of the reference's CPU path on the full workload, repeated for
+    about `budget_s` seconds with every host thread."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    x, w8, ws, bias, h, T = _cpu_reference_setup()
+    T.convrot_int8_linear_cpu(x, w8, ws, bias, h=h)  # warm the thread pool
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        T.convrot_int8_linear_cpu(x, w8, ws, bias, h=h)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return OPS * reps / el / 1e12, reps, el, cores
+
+
+def cpu_numpy_oracle_rate(rows: int, budget_s: float):
+    """TOPS of the numpy oracle's forward (the bit-exact restatement of the
+    kernels' arithmetic) on `rows` rows of the workload, for context."""
+    from oracle import convrot_oracle as O
+    x, w, _ = _cpu_inputs(rows)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    w8, ws = O.prepare_weight(w.view(torch.int16).numpy().view(np.uint16))
+    O.linear(xb[:8], w8, ws)
     reps, t0 = 0, time.perf_counter()
     while True:
         O.linear(xb, w8, ws)
@@ -178,31 +223,28 @@ def run_reference(args):
         return 0
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    rows = 128
-    from oracle import convrot_oracle as O
-    xb, wb = _cpu_inputs(rows)
-    w8, wsc = O.prepare_weight(wb)
+    x, w8, wsc, bias, h, T = _cpu_reference_setup()
     for _ in range(max(1, args.warmup)):
-        O.linear(xb, w8, wsc)
+        T.convrot_int8_linear_cpu(x, w8, wsc, bias, h=h)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.linear(xb, w8, wsc)
+        T.convrot_int8_linear_cpu(x, w8, wsc, bias, h=h)
     el = time.perf_counter() - t0
-    value = 2.0 * rows * N * K * args.steps / el / 1e12
-    sample = (f"{rows} of the 2048 rows per step (same K, N, weight); the CPU oracle "
-              f"(numpy restatement of the reference path, float64 BLAS for the exact "
-              f"int8 GEMM)")
+    value = OPS * args.steps / el / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded N(0,1) x, N(0,0.02) W)",
-        "config": {"workload": WORKLOAD, "rows_per_step": rows, "M": M, "K": K, "N": N},
+        "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) x with 1% outlier channels x10, N(0,0.02) W)",
+        "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N},
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
-                         "sample": sample},
+                         "sample": REF_SAMPLE},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("the reference's device library is SYCL for Intel Xe2 and cannot be built or "
-                 "run here; its CPU path is timed through the oracle port"),
+                 "run here; its plain-PyTorch CPU path is timed (the op sequence of "
+                 "reference/convrot_linear.py, restated because the reference tree does not "
+                 "travel to the GPU box)"),
     }
     print(json.dumps(line))
     return 0
@@ -220,7 +262,8 @@ def run_gpu(args):
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     lib = L._lib()
     stream = torch.cuda.current_stream(dev)
@@ -261,31 +304,38 @@ def run_gpu(args):
         if not np.array_equal(got, ref):
             raise RuntimeError("bench output differs from the oracle on sampled rows")
 
-    # CUDA graphs of the step over the buffer sets (capture on a side stream)
-    per_graph = NSETS * 10
+    # CUDA graphs of exactly the timed launches (captured on a side stream):
+    # one of min(K, 600) steps, replayed, and one of the remainder
+    per_graph = min(args.steps, 600)
+    full_reps, rest = divmod(args.steps, per_graph)
     capture_stream = torch.cuda.Stream(dev)
-    capture_stream.wait_stream(stream)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(capture_stream):
-        csptr = L._stream(dev)
-        with torch.cuda.graph(graph, stream=capture_stream):
-            for j in range(per_graph):
-                s = sets[j % NSETS]
-                rc = lib.xpuint8_linear_stream(csptr, L._ptr(s["x"]), L._ptr(s["w8"]),
-                                               L._ptr(s["ws"]), L._ptr(s["bias"]),
-                                               L._ptr(s["out"]), L._ptr(s["xq"]),
-                                               L._ptr(s["xs"]), M, N, K, 0)
-                if rc != 0:
-                    raise RuntimeError(lib.xpuint8_last_error())
-    stream.wait_stream(capture_stream)
+
+    def capture(nsteps):
+        graph = torch.cuda.CUDAGraph()
+        capture_stream.wait_stream(stream)
+        with torch.cuda.stream(capture_stream):
+            csptr = L._stream(dev)
+            with torch.cuda.graph(graph, stream=capture_stream):
+                for j in range(nsteps):
+                    s = sets[j % NSETS]
+                    rc = lib.xpuint8_linear_stream(csptr, L._ptr(s["x"]), L._ptr(s["w8"]),
+                                                   L._ptr(s["ws"]), L._ptr(s["bias"]),
+                                                   L._ptr(s["out"]), L._ptr(s["xq"]),
+                                                   L._ptr(s["xs"]), M, N, K, 0)
+                    if rc != 0:
+                        raise RuntimeError(lib.xpuint8_last_error())
+        stream.wait_stream(capture_stream)
+        return graph
+
+    graphs = [capture(per_graph)] + ([capture(rest)] if rest else [])
     torch.cuda.synchronize()
 
-    def run_steps(n):
-        full, rest = divmod(n, per_graph)
-        for _ in range(full):
-            graph.replay()
-        for j in range(rest):
-            step(sets[j % NSETS])
+    def run_region():
+        """exactly K steps: the main graph full_reps times, then the remainder"""
+        for _ in range(full_reps):
+            graphs[0].replay()
+        if rest:
+            graphs[1].replay()
 
     def barrier():
         if ws > 1:
@@ -293,22 +343,41 @@ def run_gpu(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    run_steps(max(3, args.warmup))
+    for _ in range(max(3, args.warmup)):  # warm-up steps (untimed)
+        step(sets[_ % NSETS])
+    run_region()
     barrier()
+    # R repetitions of the K-step region, sized on rank 0's first region and
+    # agreed over the ranks (every rank runs the same number)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier()
-        e0.record(stream)
-        run_steps(args.steps)
-        e1.record(stream)
-        e1.synchronize()
-        barrier()
-    t_ms = e0.elapsed_time(e1)
+    e0.record(stream)
+    run_region()
+    e1.record(stream)
+    e1.synchronize()
+    first_ms = e0.elapsed_time(e1)
+    reps = int(min(5000, max(3, 2500.0 / max(first_ms, 1e-3))))
     if ws > 1:
         import torch.distributed as dist
-        tt = torch.tensor([t_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_ms = float(tt.item())
+        rt = torch.tensor([reps], device=dev, dtype=torch.int64)
+        dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        reps = int(rt.item())
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    with ClockSampler(local) as clk:
+        barrier()
+        for r in range(reps):
+            starts[r].record(stream)
+            run_region()
+            ends[r].record(stream)
+        ends[-1].synchronize()
+        barrier()
+    region_ms = torch.tensor([starts[r].elapsed_time(ends[r]) for r in range(reps)],
+                             dtype=torch.float64, device=dev)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.all_reduce(region_ms, op=dist.ReduceOp.MAX)  # per repetition, the slowest rank
+    region_ms = region_ms.cpu()
+    t_ms = float(region_ms.median().item())
     value = OPS * args.steps * ws / (t_ms * 1e-3) / 1e12
     clocks = clk.summary()
 
@@ -332,25 +401,133 @@ def run_gpu(args):
                    "parallelism": f"M-shard x{ws} (replicated weights, no collective)",
                    "l2": f"{NSETS} rotating buffer sets, "
                          f"{NSETS * (M * K * 3 + N * K + M * N * 2) / 1e6:.0f} MB > 126 MB L2",
-                   "timing": "CUDA-graph replay of the same launches; eager launches in "
-                             "eager_ms_per_step"},
+                   "timing": (f"each timed region is exactly {args.steps} steps replayed from CUDA "
+                              f"graphs of those launches; {reps} regions back to back, each timed "
+                              f"by CUDA events (max over ranks); ms_per_step = median region / "
+                              f"steps; eager launches in eager_ms_per_step")},
+        "repeats": reps,
+        "region_ms": {"median": t_ms, "min": float(region_ms.min().item()),
+                      "max": float(region_ms.max().item())},
         "eager_ms_per_step": eager_ms,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * args.steps * reps,
         "clocks": clocks,
     }
+    del graphs
 
     if rank == 0:
         result.update(_rank0_extras(args, lib, L, dev, sets, stream))
+    del sets
+    torch.cuda.empty_cache()
+    # config C5 at N ranks: M-sharded (every rank), then the N-sharded all-gather
+    result["c5_mshard"] = _c5_mshard(args, dev, stream, ws, rank)
+    if ws > 1:
+        result["c5_nshard"] = _c5_nshard(args, dev, stream, ws, rank)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
-    del graph
-    if ws > 1:
-        import torch.distributed as dist
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))
     return 0
+
+
+def _timed_max(fn, steps, stream, ws, dev):
+    """Device time of `steps` calls (ms), max over ranks, after a barrier."""
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _c5_mshard(args, dev, stream, ws, rank):
+    """Config C5 M-sharded: 65536 rows of x [., 4096] split over the ranks, the
+    [4096,4096] and [14336,4096] weights replicated; whole-job TOPS =
+    2 * 65536 * N * 4096 / the slowest rank's time (strong scaling)."""
+    import xpu_kernels
+    from xpu_kernels.int8 import shard
+    r0, r1 = shard.row_range(C5_M, ws, rank)
+    g = torch.Generator(device=dev).manual_seed(40 + rank)
+    x = torch.randn(r1 - r0, C5_K, generator=g, device=dev)
+    x[:, :20] *= 20
+    x = x.to(torch.bfloat16)
+    out = {}
+    steps = max(3, min(args.steps, 50))
+    for n in (4096, 14336):
+        gw = torch.Generator(device=dev).manual_seed(n)
+        w = (torch.randn(n, C5_K, generator=gw, device=dev) * 0.02).to(torch.bfloat16)
+        w8, wsc = xpu_kernels.prepare_weight(w)
+        del w
+        y = torch.empty(r1 - r0, n, dtype=torch.bfloat16, device=dev)
+        xq = torch.empty(r1 - r0, C5_K, dtype=torch.int8, device=dev)
+        xs = torch.empty(r1 - r0, dtype=torch.float32, device=dev)
+        from xpu_kernels.int8 import _lib as L
+        lib = L._lib()
+        sp = L._stream(dev)
+
+        def fn(_):
+            rc = lib.xpuint8_linear_stream(sp, L._ptr(x), L._ptr(w8), L._ptr(wsc), None, L._ptr(y),
+                                           L._ptr(xq), L._ptr(xs), r1 - r0, n, C5_K, 0)
+            if rc != 0:
+                raise RuntimeError(lib.xpuint8_last_error())
+        for i in range(3):
+            fn(i)
+        t = _timed_max(fn, steps, stream, ws, dev) / steps
+        out[f"w{n}"] = {"ms_per_step": t, "tops": 2.0 * C5_M * n * C5_K / (t * 1e-3) / 1e12,
+                        "rows_per_rank": r1 - r0}
+        del w8, wsc, y, xq, xs
+    out["shape"] = (f"x bf16 [{C5_M},{C5_K}] split over {ws} rank(s) by rows; weights "
+                    f"[4096,4096] and [14336,4096] replicated; {steps} steps timed, max over ranks")
+    del x
+    torch.cuda.empty_cache()
+    return out
+
+
+def _c5_nshard(args, dev, stream, ws, rank):
+    """Config C5's N-sharded variant at N ranks: x [65536,4096] on every rank,
+    [14336,4096] split by output channels; the fused form stores every output
+    tile into every rank's buffer over NVLink (no multicast), the NCCL form
+    all-gathers the blocks.  Whole-job TOPS, strong scaling."""
+    import xpu_kernels
+    from xpu_kernels.int8 import shard
+    m, n = C5_M, 14336
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn(m, C5_K, generator=g, device=dev)
+    x[:, :20] *= 20
+    x = x.to(torch.bfloat16)
+    w = (torch.randn(n, C5_K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w8, wsc = xpu_kernels.prepare_weight(w)
+    del w
+    w8l, wsl, _ = shard.shard_weight(w8, wsc, ws, rank)
+    del w8, wsc
+    peer = shard.PeerOutput(m, n)
+    steps = max(3, min(args.steps, 20))
+    try:
+        y_f = shard.linear_nshard_fused(x, w8l, wsl, None, peer).clone()
+        y_n = shard.linear_nshard(x, w8l, wsl, None, n_total=n)
+        same = bool(torch.equal(y_f.view(torch.int16), y_n.view(torch.int16)))
+        del y_f, y_n
+        t_f = _timed_max(lambda i: shard.linear_nshard_fused(x, w8l, wsl, None, peer), steps,
+                         stream, ws, dev) / steps
+        t_n = _timed_max(lambda i: shard.linear_nshard(x, w8l, wsl, None, n_total=n), steps,
+                         stream, ws, dev) / steps
+    finally:
+        peer.close()
+    ops_ = 2.0 * m * n * C5_K
+    return {"fused_allgather_ms": t_f, "fused_tops": ops_ / (t_f * 1e-3) / 1e12,
+            "nccl_allgather_ms": t_n, "nccl_tops": ops_ / (t_n * 1e-3) / 1e12,
+            "forms_bit_identical": same,
+            "output_bytes_sent_per_rank": m * (n // ws) * 2 * (ws - 1),
+            "shape": f"x bf16 [{m},{C5_K}] on every rank, W [{n},{C5_K}] split over {ws} ranks"}
 
 
 def _time_launches(fn, n, stream):
@@ -407,6 +584,26 @@ def _rank0_extras(args, lib, L, dev, sets, stream):
         out["roofline"]["cublaslt_int_mm_tops"] = OPS / (t_cub * 1e-3) / 1e12
     except Exception as exc:  # noqa: BLE001 - context only
         out["roofline"]["cublaslt_int_mm_tops"] = f"unavailable: {exc}"
+    # a measured int8 dense peak: cuBLASLt's int8 GEMM at 8192^3 (burst, best of
+    # 20 launches), the denominator of `frac_of_measured_int8`
+    try:
+        g8 = torch.Generator(device=dev).manual_seed(8)
+        a8 = torch.randint(-127, 128, (8192, 8192), generator=g8, device=dev, dtype=torch.int8)
+        b8 = torch.randint(-127, 128, (8192, 8192), generator=g8, device=dev, dtype=torch.int8)
+        bt = b8.t()
+        for _ in range(3):
+            torch._int_mm(a8, bt)
+        best = None
+        for _ in range(20):
+            t = _time_launches(lambda i: torch._int_mm(a8, bt), 1, stream)
+            best = t if best is None else min(best, t)
+        peak8 = 2.0 * 8192 ** 3 / (best * 1e-3) / 1e12
+        out["roofline"]["int8_measured_peak"] = {
+            "tops": peak8, "how": "cuBLASLt int8 GEMM (torch._int_mm) 8192^3, best of 20"}
+        out["roofline"]["frac_of_measured_int8"] = achieved / peak8
+        del a8, b8, bt
+    except Exception as exc:  # noqa: BLE001 - context only
+        out["roofline"]["int8_measured_peak"] = f"unavailable: {exc}"
 
     # rotate+quantize at config C5, the HBM-bound half of the metric
     del_sets = []
@@ -494,14 +691,17 @@ def _rank0_extras(args, lib, L, dev, sets, stream):
                   "api": ("xpu_kernels.linear (pinned host in/out; host->device copy, linear "
                           "and device->host copy on three streams, consecutive steps overlapped)")}
 
-    # the CPU baseline: the oracle on a row sample
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    rate, reps, el = cpu_oracle_rate(128, budget_s=float(os.environ.get("CPU_BASELINE_S", "10")))
+    # the CPU baseline: the reference's CPU path on the full workload, and the
+    # numpy oracle on a row sample for context
+    budget = float(os.environ.get("CPU_BASELINE_S", "10"))
+    rate, reps, el, cores = cpu_reference_rate(budget)
+    nrate, nreps, nel = cpu_numpy_oracle_rate(128, budget_s=min(5.0, budget))
     out["cpu_baseline"] = {
         "value": rate, "unit": "TOPS", "cores": cores, "kind": "port",
-        "sample": (f"128 of the 2048 rows x {reps} repetitions ({el:.1f} s): the CPU oracle "
-                   f"(numpy restatement of the reference path, float64 BLAS GEMM)")}
+        "sample": f"{REF_SAMPLE}; {reps} steps in {el:.1f} s",
+        "numpy_oracle": {"value": nrate, "unit": "TOPS",
+                         "sample": (f"128 of the 2048 rows x {nreps} repetitions ({nel:.1f} s): "
+                                    f"the bit-exact numpy restatement, float64 BLAS GEMM")}}
     return out
 
 

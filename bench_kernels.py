@@ -1,26 +1,32 @@
-"""Run one kernel of the library on one shape, for profiling and quick timing.
+"""Per-kernel benchmark harness: one kernel of the library on one shape.
 
-    python -m xpu_kernels.int8.cases gemm --M 2048 --N 10240 --K 1280 --iters 20
-    python -m xpu_kernels.int8.cases rotate_quant --M 65536 --K 4096
-    python -m xpu_kernels.int8.cases linear | ffn | dx | dw | quantize_row | dequant
-    python -m xpu_kernels.int8.cases suite [--iters N]   (every shape of SUITE)
+    python bench_kernels.py gemm --M 2048 --N 10240 --K 1280 --iters 20
+    python bench_kernels.py rotate_quant --M 65536 --K 4096
+    python bench_kernels.py linear | ffn | dx | dw | quantize_row | dequant | ...
+    python bench_kernels.py suite [--iters N]   (every shape of SUITE, timing only)
 
 Inputs are seeded and generated on the device; each case launches its kernel
 `--iters` times over `--sets` rotating buffer sets and prints the average
-device time per launch (CUDA events) with the algorithmic throughput.  It is
-the driver the committed ncu summaries name (profile one launch with
-``ncu -k regex:<kernel> -s <skip> -c 1``).
+device time per launch (CUDA events) with the algorithmic throughput.  The
+ncu summaries under profiles/ each name the single-case command they came
+from, captured one kernel at a time (``ncu -k regex:<kernel> -s <skip> -c 1``)
+on a small case.  ``bench.py`` is the headline benchmark; this file is for the
+individual kernels.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import torch
 
-from . import ops
-from ._lib import _lib, _ptr, _stream
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "oko-xpu-kernels_b200"))
+
+from xpu_kernels.int8 import ops  # noqa: E402
+from xpu_kernels.int8._lib import _lib, _ptr, _stream  # noqa: E402
 
 
 def _time(fn, iters, stream):
@@ -36,9 +42,9 @@ def _time(fn, iters, stream):
     return e0.elapsed_time(e1) / iters
 
 
-# The shapes the committed ncu summaries cover (BASELINE configs C3 W1, C3
-# GEGLU, C4 backward, C5), run by ``cases suite`` in one process: each case
-# launches its kernels ``--iters`` times (profile with a kernel-name filter).
+# The shapes of the BASELINE configs (C3 W1, C3 GEGLU, C4 backward, C5), run by
+# ``suite`` in one process for timing.  Profile one case at a time, never the
+# suite (it holds up to a few GB and runs every kernel).
 SUITE = [
     ["gemm", "--M", "2048", "--N", "10240", "--K", "1280", "--sets", "6"],
     ["geglu", "--M", "2048", "--N", "5120", "--K", "1280", "--sets", "6"],

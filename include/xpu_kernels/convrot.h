@@ -161,9 +161,21 @@ int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *
 int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_scale, int8_t *gq,
                             float *tg, int64_t M, int64_t N);
 
-/* The device fault word of the GEMM's bounded waits (0 = none), read with a
- * device synchronisation; reset != 0 clears it. */
+/* The device fault words of the bounded waits (0 = none: the GEMM's, then the
+ * wait probe's), read with a device synchronisation; reset != 0 clears them.
+ * A GEMM wait that gave up records its site here and the kernel returns. */
 int xpuint8_fault_status(int32_t reset);
+
+/* Self-test of the bounded device waits (blocking, legacy default stream):
+ * one CTA waits on a shared-memory mbarrier that nothing arrives on, through
+ * the GEMM's own bounded wait, with a limit of limit_ns (clamped to
+ * [1 us, 2 s]).  The wait gives up, records `site` (non-zero) in the fault
+ * word xpuint8_fault_status reports, and the kernel returns; *elapsed_ns
+ * (if not NULL) receives how long it waited.  The probe's word is separate
+ * from the GEMM's, so it never stops a later GEMM.  No counterpart in the
+ * reference, whose failure model is the return code and last-error text
+ * (src/xpuint8.cpp:47-50). */
+int xpuint8_wait_probe(int64_t limit_ns, int32_t site, int64_t *elapsed_ns);
 
 /* The N-sharded INT8 linear with its output all-gather fused into the GEMM
  * (BASELINE config C5's large-weight variant; the reference has no
@@ -182,6 +194,18 @@ int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int
                                     const float *w_scale, const float *bias, void *const *outs,
                                     int32_t nranks, int32_t rank, int8_t *xq, float *xs, int64_t M,
                                     int64_t N, int64_t K, int32_t activation);
+
+/* The same with the column block given explicitly, for blocks of unequal
+ * width (N output columns not divisible into equal multiple-of-16 blocks):
+ * this rank's tiles land at columns [col_offset, col_offset + N) of every
+ * rank's [M, n_total] output.  col_offset and n_total are multiples of 16.
+ * xpuint8_linear_allgather_stream is this call with col_offset = rank * N and
+ * n_total = nranks * N. */
+int xpuint8_linear_allgather_cols_stream(const void *stream, const void *x, const int8_t *w8,
+                                         const float *w_scale, const float *bias,
+                                         void *const *outs, int32_t nranks, int64_t col_offset,
+                                         int64_t n_total, int8_t *xq, float *xs, int64_t M,
+                                         int64_t N, int64_t K, int32_t activation);
 
 /* Peer-visible device buffers for the fused all-gather (set-up time, not per
  * call): xpuint8_ipc_alloc allocates `bytes` on the current device and
@@ -210,8 +234,9 @@ int xpuint8_check_scale_math(int64_t *bad_scale, int64_t *bad_quant);
  * library (8 MiB + 64 KiB, held on every GPU that loads the library until
  * exit), so M <= 16384 and M * K <= 8 MiB; larger calls return 2.  All calls
  * on a device share that array: calls whose work overlaps on the GPU race.
- * The first call on a device resolves the array's address (and may load the
- * library's device code); make it before any stream capture. */
+ * The first call on a device (in each CUDA context there: a device reset or
+ * another current context looks it up anew) resolves the array's address and
+ * may load the library's device code; make it before any stream capture. */
 int xpuint8_linear_noalloc_stream(const void *stream, const void *x, const int8_t *w8,
                                   const float *w_scale, const float *bias, void *out, int64_t M,
                                   int64_t N, int64_t K, int32_t activation);

@@ -500,9 +500,18 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
 
 int xpuint8_fault_status(int32_t reset) {
     const int g = gemm_fault_status(reset);
-    const int r = rot_fault_status(reset);
+    const int r = probe_fault_status(reset);
     if (g < 0 || r < 0) return -1;
     return g != 0 ? g : r;
+}
+
+int xpuint8_wait_probe(int64_t limit_ns, int32_t site, int64_t *elapsed_ns) {
+    if (xpuint8_init() != 0) return 1;
+    if (site == 0) {
+        set_error("wait_probe: the site must be non-zero");
+        return 2;
+    }
+    return launch_wait_probe(limit_ns, site, elapsed_ns);
 }
 
 // ---------------------------------------------------------------- peer buffers
@@ -564,16 +573,22 @@ int xpuint8_ipc_free(void *ptr) {
     return 0;
 }
 
-int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int8_t *w8,
-                                    const float *w_scale, const float *bias, void *const *outs,
-                                    int32_t nranks, int32_t rank, int8_t *xq, float *xs, int64_t M,
-                                    int64_t N, int64_t K, int32_t activation) {
+int xpuint8_linear_allgather_cols_stream(const void *stream, const void *x, const int8_t *w8,
+                                         const float *w_scale, const float *bias,
+                                         void *const *outs, int32_t nranks, int64_t col_offset,
+                                         int64_t n_total, int8_t *xq, float *xs, int64_t M,
+                                         int64_t N, int64_t K, int32_t activation) {
     if (N <= 0 || N % 16 != 0) {
         set_error("N (this rank's columns) must be a positive multiple of 16");
         return 2;
     }
-    if (!outs || nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) {
-        set_error("allgather: 1 <= nranks <= 8, 0 <= rank < nranks and an output table are required");
+    if (!outs || nranks < 1 || nranks > 8) {
+        set_error("allgather: 1 <= nranks <= 8 and an output table are required");
+        return 2;
+    }
+    if (n_total % 16 != 0 || col_offset < 0 || col_offset % 16 != 0 || col_offset + N > n_total) {
+        set_error("allgather: the column block [col_offset, col_offset + N) must lie inside the "
+                  "n_total output columns, with col_offset and n_total multiples of 16");
         return 2;
     }
     void *dst[8];
@@ -582,8 +597,8 @@ int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int
             set_error("allgather: every output buffer needs a 16-byte aligned base");
             return 2;
         }
-        // this rank's column block of rank r's [M, nranks * N] output
-        dst[r] = static_cast<char *>(outs[r]) + static_cast<int64_t>(rank) * N * 2;
+        // this rank's column block of rank r's [M, n_total] output
+        dst[r] = static_cast<char *>(outs[r]) + col_offset * 2;
     }
     if (!w8 || !w_scale || !aligned16(w8)) {
         set_error("a required pointer is null or misaligned");
@@ -594,11 +609,25 @@ int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int
     // 128-byte row segments per store: the tiles cross NVLink in larger writes
     c.epilogue = kEpiDequantWide;
     c.a = xq; c.b = w8; c.lda = K; c.ldb = K;
-    c.outs = dst; c.nout = nranks; c.ldo = static_cast<int64_t>(nranks) * N;
+    c.outs = dst; c.nout = nranks; c.ldo = n_total;
     c.row_scale = xs; c.col_scale = w_scale; c.bias = bias;
     c.M = M; c.N = N; c.K = K;
     c.b_early = true;  // the quantizer above is the kernel just before
     return launch_gemm(as_stream(stream), c);
+}
+
+int xpuint8_linear_allgather_stream(const void *stream, const void *x, const int8_t *w8,
+                                    const float *w_scale, const float *bias, void *const *outs,
+                                    int32_t nranks, int32_t rank, int8_t *xq, float *xs, int64_t M,
+                                    int64_t N, int64_t K, int32_t activation) {
+    if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) {
+        set_error("allgather: 1 <= nranks <= 8 and 0 <= rank < nranks are required");
+        return 2;
+    }
+    return xpuint8_linear_allgather_cols_stream(stream, x, w8, w_scale, bias, outs, nranks,
+                                                static_cast<int64_t>(rank) * N,
+                                                static_cast<int64_t>(nranks) * N, xq, xs, M, N, K,
+                                                activation);
 }
 
 int xpuint8_check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {

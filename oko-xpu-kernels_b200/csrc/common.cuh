@@ -116,20 +116,22 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
-// A wait that always ends.  It gives up after kWaitTimeoutNs of wall time (or
-// kWaitMaxIters polls), records `site` in *fault (first writer wins) and
-// returns false; it also returns false as soon as another thread has recorded
-// a fault, so every role of every CTA leaves its loop within a bounded time.
+// A wait that always ends.  It gives up after timeout_ns of wall time (2 s
+// unless given; or kWaitMaxIters polls), records `site` in *fault (first
+// writer wins) and returns false; it also returns false as soon as another
+// thread has recorded a fault, so every role of every CTA leaves its loop
+// within a bounded time.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 constexpr uint32_t kWaitMaxIters = 1u << 28;
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *fault, int site) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *fault, int site,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1; it < kWaitMaxIters; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0u) {
             if (*reinterpret_cast<volatile int *>(fault) != 0) return false;
-            if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
+            if (global_timer_ns() - t0 > timeout_ns) break;
         }
     }
     atomicCAS(fault, 0, site);

@@ -619,19 +619,21 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
     return true;
 }
 
-// CTA pairs that can be resident at once for this kernel (cached per device)
+// CTA pairs that can be resident at once for this kernel (the occupancy is
+// cached per device; the shared-memory attribute is set on every call, so a
+// device reset, which clears it, cannot leave a launch without it)
 template <int EPI, bool A_MN, bool B_MN>
 int resident_pairs(int dev) {
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
+        return -1;
     // atomic: first calls from several host threads may race to fill it (same value)
     static std::atomic<int> cached[32] = {};
     if (dev >= 0 && dev < 32) {
         const int c = cached[dev].load(std::memory_order_relaxed);
         if (c > 0) return c;
     }
-    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
-        return -1;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -25,7 +25,6 @@ int launch_rotate_rows(cudaStream_t s, int mode, int act, const void *in, const 
 // mode 3's weight scale, mode 1's x_scale; col_scale: mode 1's w_scale
 int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const float *row_scale,
                        const float *col_scale, void *out, float *scale, int64_t M, int64_t K);
-int rot_fault_status(int reset);  // device fault word of the streaming rotation's waits
 // self-check of the quantizers' scale arithmetic (rotate_bulk.cu); counts mismatches
 int check_scale_math(int64_t *bad_scale, int64_t *bad_quant);
 
@@ -66,5 +65,10 @@ struct GemmCall {
 };
 int launch_gemm(cudaStream_t s, const GemmCall &c);
 int gemm_fault_status(int reset);  // device fault word of the GEMM waits
+
+// the bounded-wait self-test (waitprobe.cu): one CTA waits on an mbarrier that
+// nothing arrives on, gives up after limit_ns and records `site`
+int launch_wait_probe(int64_t limit_ns, int site, int64_t *elapsed_ns);
+int probe_fault_status(int reset);  // its fault word
 
 }  // namespace xpuint8

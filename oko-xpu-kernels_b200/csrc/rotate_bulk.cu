@@ -6,12 +6,12 @@
 //   mode 3  int8 [N,K] * scale [N] -> bf16 -> rotate -> bf16 [N,K]
 //           (dequant_weight_torch, python/xpu_kernels/int8/ops.py:169-191)
 //
-// Persistent CTAs walk "batches" of R consecutive rows.  A batch is contiguous
-// in HBM, so one thread moves it into shared memory with a single 1-D bulk
-// copy (cp.async.bulk ... mbarrier::complete_tx), NS batches ahead of the
-// compute; the result is staged in shared memory in its final order and
-// leaves with one bulk store.  No global load or store instruction touches the
-// data itself, and the copy engine keeps NS x batch bytes in flight per CTA.
+// Two kernels.  rotate_direct_kernel (K <= 8192, every shape the linear
+// entries meet) is described above it.  rotate_bulk_kernel serves longer rows
+// (K up to 32768 in slots of 1, 2 or 4 pairs of groups): persistent CTAs walk
+// "batches" of R consecutive rows, load each group straight from global memory
+// into registers, and stage the result in shared memory in its final order, so
+// that a batch leaves with one bulk store (cp.async.bulk) per CTA.
 //
 // Arithmetic: a half-warp ("slot") owns PAIRS of 256-groups and processes the
 // two groups of a pair together as packed fp32x2 values, so every butterfly
@@ -25,16 +25,13 @@
 //
 // Row abs-max: per-group maxima go through shared-memory atomics into a
 // triple-buffered per-row array; quantization (reciprocal multiply, RNE by an
-// fp32 magic add) happens after one CTA barrier.
-//
-// All waits are bounded (common.cuh: mbar_wait); on a timeout the CTA records
-// the site in g_rot_fault, drains its own bulk copies and returns.
+// fp32 magic add) happens after one CTA barrier.  Neither kernel waits on an
+// mbarrier or on another CTA: every barrier is a CTA barrier.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
-#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -42,21 +39,10 @@
 
 namespace xpuint8 {
 
-__device__ int g_rot_fault = 0;
-
 namespace {
 
 constexpr int kSlots = 16;             // half-warps per 256-thread CTA
-// Input path: direct 16-byte loads into registers (default), or bulk copies
-// into shared-memory stages (the form this file started from, kept for A/B
-// builds with -DXPUINT8_ROTATE_STAGED).  The direct form needs no input
-// staging, so more CTAs fit per SM; the kernel is latency-bound, not
-// bandwidth-bound, at the staged form's occupancy.
-#ifdef XPUINT8_ROTATE_STAGED
-constexpr bool kDirect = false;
-#else
-constexpr bool kDirect = true;
-#endif
+constexpr int kCacheDevices = 64;      // devices whose occupancy is cached
 constexpr int kTileBytes = 16 * 128;   // 16 rows x 16 fp32x2 per slot
 
 struct BulkParams {
@@ -66,9 +52,9 @@ struct BulkParams {
     uint8_t *out;
     float *scale;            // mode 0: per-row output scale
     int64_t M, K;
-    int G, R, nbatch, ns, os;  // os: output stages (1 or 2)
+    int G, R, nbatch, os;    // os: output stages (1 or 2)
     uint32_t in_row_bytes, out_row_bytes;
-    uint32_t in_stage_bytes, out_stage_bytes;
+    uint32_t out_stage_bytes;
 };
 
 __device__ __forceinline__ float gelu_erf_f(float x) {
@@ -107,42 +93,7 @@ __device__ __forceinline__ float activate(float a, float b) {
 }
 __host__ __device__ constexpr bool act_paired(int act) { return act == 2 || act == 3 || act == 4; }
 
-// the 16 values lane l owns of one group, from the staged batch
-template <int MODE, int ACT>
-__device__ __forceinline__ void load16(const BulkParams &p, uint32_t stage, int rib, int g, int l,
-                                       float (&v)[16]) {
-    if constexpr (MODE == 3) {
-        const uint4 b = *reinterpret_cast<const uint4 *>(
-            __cvta_shared_to_generic(stage + rib * p.in_row_bytes + g * 256 + l * 16));
-        const float s = __ldg(p.row_scale + rib);  // rebased by the caller
-        const uint32_t w[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-                v[4 * j + t] = round_bf16(
-                    __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * t)) & 0xFF)), s));
-    } else {
-        const uint8_t *base = reinterpret_cast<const uint8_t *>(
-            __cvta_shared_to_generic(stage + rib * p.in_row_bytes + (g * 256 + l * 16) * 2));
-        const uint4 a0 = *reinterpret_cast<const uint4 *>(base);
-        const uint4 a1 = *reinterpret_cast<const uint4 *>(base + 16);
-        unpack16_bf16(a0, a1, v);
-        if constexpr (MODE == 0 && act_paired(ACT)) {
-            const uint4 b0 = *reinterpret_cast<const uint4 *>(base + p.K * 2);
-            const uint4 b1 = *reinterpret_cast<const uint4 *>(base + p.K * 2 + 16);
-            float u[16];
-            unpack16_bf16(b0, b1, u);
-#pragma unroll
-            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], u[t]);
-        } else if constexpr (MODE == 0 && ACT != 0) {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) v[t] = activate<ACT>(v[t], 0.f);
-        }
-    }
-}
-
-// the same 16 values loaded straight from global memory (row = absolute row)
+// the 16 values lane l owns of one group, loaded from global memory (row = absolute row)
 template <int MODE, int ACT>
 __device__ __forceinline__ void load16_global(const BulkParams &p, int64_t row, int g, int l,
                                               float (&v)[16]) {
@@ -230,29 +181,20 @@ __device__ __forceinline__ float halfwarp_max(float v) {
     return v;
 }
 
-template <int MODE, int ACT, int PPS, bool DIRECT>
+template <int MODE, int ACT, int PPS>
 __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(const BulkParams p) {
     constexpr bool QUANT = (MODE == 0);
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t s0 = smem_u32(smem);
-    const uint32_t in_base = s0;
-    // the direct-load form has no input stages: its shared memory starts with
-    // the output stages (the host sizes it the same way)
-    const uint32_t out_base = in_base + (DIRECT ? 0u : p.ns * p.in_stage_bytes);
+    // shared memory: the output stages, the slots' transpose tiles, the row maxima
+    const uint32_t out_base = smem_u32(smem);
     const uint32_t tile_base = out_base + p.os * p.out_stage_bytes;
-    unsigned int *row_amax = reinterpret_cast<unsigned int *>(smem + (tile_base - s0) + kSlots * kTileBytes);
-    uint64_t *fullb = reinterpret_cast<uint64_t *>(row_amax + 3 * 32);
-    const uint32_t full0 = smem_u32(fullb);
-    int *fault = &g_rot_fault;
+    unsigned int *row_amax =
+        reinterpret_cast<unsigned int *>(smem + p.os * p.out_stage_bytes + kSlots * kTileBytes);
 
     const int slot = threadIdx.x >> 4, l = threadIdx.x & 15;
     const uint32_t tile = tile_base + slot * kTileBytes;
     const int groups = p.R * p.G;
 
-    if (!DIRECT && threadIdx.x == 0) {
-        for (int s = 0; s < p.ns; ++s) mbar_init(full0 + 8 * s, 1);
-        fence_mbar_init();
-    }
     if (threadIdx.x < 3 * 32) row_amax[threadIdx.x] = 0u;
     __syncthreads();
 
@@ -261,32 +203,11 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
         const int64_t left = p.M - r0;
         return static_cast<int>(left < p.R ? left : p.R);
     };
-    auto issue = [&](int k) {  // batch k of this CTA into stage k % ns
-        const int b = blockIdx.x + k * gridDim.x;
-        if (b >= p.nbatch) return false;
-        const uint32_t bytes = batch_rows(b) * p.in_row_bytes;
-        const uint32_t bar = full0 + 8 * (k % p.ns);
-        mbar_expect_tx(bar, bytes);
-        bulk_load(in_base + (k % p.ns) * p.in_stage_bytes,
-                  p.in + static_cast<int64_t>(b) * p.R * p.in_row_bytes, bytes, bar);
-        return true;
-    };
-    int issued = 0;
-    if (!DIRECT && threadIdx.x == 0)
-        for (int k = 0; k < p.ns; ++k) issued += issue(k) ? 1 : 0;
 
     int k = 0;
     for (int b = blockIdx.x; b < p.nbatch; b += gridDim.x, ++k) {
-        const int st = DIRECT ? 0 : k % p.ns;
         const int rows = batch_rows(b);
         const int64_t row0 = static_cast<int64_t>(b) * p.R;
-        // every thread waits (acquiring the copy), and the CTA leaves together
-        // if any wait gave up
-        if constexpr (!DIRECT) {
-            const bool ok = mbar_wait(full0 + 8 * st, (k / p.ns) & 1, fault, 21);
-            if (!__syncthreads_and(ok)) break;
-        }
-        const uint32_t stage = in_base + st * p.in_stage_bytes;
         unsigned int *amax_now = row_amax + 32 * (k % 3);
 
         f2 vals[PPS][16];
@@ -298,29 +219,13 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
             const bool v0 = f0 < groups && r0 < rows, v1 = f1 < groups && r1 < rows;
             float a[16], c[16];
             if (v0) {
-                if constexpr (DIRECT) {
-                    load16_global<MODE, ACT>(p, row0 + r0, g0, l, a);
-                } else if constexpr (MODE == 3) {
-                    BulkParams q = p;
-                    q.row_scale = p.row_scale + row0;
-                    load16<MODE, ACT>(q, stage, r0, g0, l, a);
-                } else {
-                    load16<MODE, ACT>(p, stage, r0, g0, l, a);
-                }
+                load16_global<MODE, ACT>(p, row0 + r0, g0, l, a);
             } else {
 #pragma unroll
                 for (int t = 0; t < 16; ++t) a[t] = 0.f;
             }
             if (v1) {
-                if constexpr (DIRECT) {
-                    load16_global<MODE, ACT>(p, row0 + r1, g1, l, c);
-                } else if constexpr (MODE == 3) {
-                    BulkParams q = p;
-                    q.row_scale = p.row_scale + row0;
-                    load16<MODE, ACT>(q, stage, r1, g1, l, c);
-                } else {
-                    load16<MODE, ACT>(p, stage, r1, g1, l, c);
-                }
+                load16_global<MODE, ACT>(p, row0 + r1, g1, l, c);
             } else {
 #pragma unroll
                 for (int t = 0; t < 16; ++t) c[t] = 0.f;
@@ -354,7 +259,6 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
             else bulk_wait_read<0>();
         }
         __syncthreads();
-        if (!DIRECT && threadIdx.x == 0 && issue(k + p.ns)) ++issued;
 
         const uint32_t ostage = out_base + (k % p.os) * p.out_stage_bytes;
 #pragma unroll
@@ -415,16 +319,7 @@ __global__ void __launch_bounds__(256, (PPS == 1 ? 4 : 1)) rotate_bulk_kernel(co
             bulk_commit();
         }
     }
-    if (threadIdx.x == 0) {
-        // batches whose copies were issued but not consumed (after a fault)
-        for (int kk = k; kk < issued; ++kk) {
-            const uint32_t bar = full0 + 8 * (kk % p.ns);
-            const uint64_t t0 = global_timer_ns();
-            while (!mbar_try_wait(bar, (kk / p.ns) & 1))
-                if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
-        }
-        bulk_wait<0>();
-    }
+    if (threadIdx.x == 0) bulk_wait<0>();
     __syncthreads();
 }
 
@@ -766,16 +661,18 @@ int launch_direct(cudaStream_t s, const BulkParams &p) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return launch_status("rotate (shared memory attribute)");
-    // resident CTAs per SM (atomic: first calls from several host threads may
-    // race to fill it, with the same value)
-    static std::atomic<int> cached_per_sm{0};
-    int per_sm = cached_per_sm.load(std::memory_order_relaxed);
+    // resident CTAs per SM, cached per device (atomic: first calls from
+    // several host threads may race to fill it, with the same value)
+    static std::atomic<int> cached_per_sm[kCacheDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = (dev >= 0 && dev < kCacheDevices) ? cached_per_sm[dev].load(std::memory_order_relaxed) : 0;
     if (per_sm == 0) {
         int per = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, SLOTS * 16, smem) != cudaSuccess)
             per = 1;
         per_sm = std::max(1, per);
-        cached_per_sm.store(per_sm, std::memory_order_relaxed);
+        if (dev >= 0 && dev < kCacheDevices) cached_per_sm[dev].store(per_sm, std::memory_order_relaxed);
     }
     const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * per_sm);
     cudaLaunchConfig_t cfg = {};
@@ -801,37 +698,27 @@ int launch_direct(cudaStream_t s, const BulkParams &p, int slots) {
     }
 }
 
+// The kernel for longer rows.  Its shared memory depends on the batch (R
+// rows), so the occupancy is computed per launch (a host-side calculation);
+// it sizes the persistent grid only.
+template <int MODE, int ACT, int PPS>
+int launch_bulk(cudaStream_t s, const BulkParams &p, size_t smem) {
+    auto kern = rotate_bulk_kernel<MODE, ACT, PPS>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return launch_status("rotate (shared memory attribute)");
+    int per = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess) per = 1;
+    const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * std::max(1, per));
+    kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
+    return launch_status("rotate");
+}
 template <int MODE, int ACT>
-int launch_pps(cudaStream_t s, BulkParams p, int pps, size_t smem) {
-    auto pick = [&](auto kern) -> int {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)) != cudaSuccess)
-            return launch_status("rotate (shared memory attribute)");
-        // resident blocks per SM for this kernel and shared-memory size (cached;
-        // the pair is read and updated under a lock)
-        static std::mutex cache_mu;
-        static size_t cached_smem = 0;
-        static int cached_per_sm = 0;
-        int per_sm;
-        {
-            std::lock_guard<std::mutex> lock(cache_mu);
-            if (cached_smem != smem) {
-                int per = 0;
-                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem) != cudaSuccess)
-                    per = 1;
-                cached_per_sm = std::max(1, per);
-                cached_smem = smem;
-            }
-            per_sm = cached_per_sm;
-        }
-        const int64_t grid = std::min<int64_t>(p.nbatch, static_cast<int64_t>(num_sms()) * per_sm);
-        kern<<<static_cast<unsigned>(grid), 256, smem, s>>>(p);
-        return launch_status("rotate");
-    };
+int launch_pps(cudaStream_t s, const BulkParams &p, int pps, size_t smem) {
     switch (pps) {
-        case 1: return pick(rotate_bulk_kernel<MODE, ACT, 1, kDirect>);
-        case 2: return pick(rotate_bulk_kernel<MODE, ACT, 2, kDirect>);
-        case 4: return pick(rotate_bulk_kernel<MODE, ACT, 4, kDirect>);
+        case 1: return launch_bulk<MODE, ACT, 1>(s, p, smem);
+        case 2: return launch_bulk<MODE, ACT, 2>(s, p, smem);
+        case 4: return launch_bulk<MODE, ACT, 4>(s, p, smem);
         default: break;
     }
     set_error("unsupported group count per slot");
@@ -854,7 +741,7 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
         if (util >= 0.85) { pps = c; R = r; break; }
         if (util > best) { best = util; pps = c; R = r; }
     }
-    if (!(kDirect && G <= 32) && (pps == 0 || R < 1)) return -1;
+    if (G > 32 && (pps == 0 || R < 1)) return -1;
     if (R > 32) R = 32;
     if (R < 1) R = 1;
     BulkParams p{};
@@ -868,39 +755,24 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
     const int64_t in_elem = mode == 3 ? 1 : (mode == 1 ? 4 : 2);
     p.in_row_bytes = static_cast<uint32_t>(in_elem * K * (paired ? 2 : 1));
     p.out_row_bytes = static_cast<uint32_t>(mode <= 1 ? K : 2 * K);
-    auto up = [](uint32_t x) { return (x + 127u) & ~127u; };
-    p.in_stage_bytes = up(R * p.in_row_bytes);
-    p.out_stage_bytes = up(R * p.out_row_bytes);
+    p.out_stage_bytes = (R * p.out_row_bytes + 127u) & ~127u;
     const int64_t nb = (M + R - 1) / R;
     if (nb > 0x7FFFFFFF) return -1;
     p.nbatch = static_cast<int>(nb);
-    // stage counts: the most CTAs per SM (228 KB of shared memory, 1 KB reserved
-    // per CTA), then the deepest input pipeline, then double-buffered output
-    auto total = [&](int ns, int os) {
-        return static_cast<size_t>(ns) * p.in_stage_bytes + static_cast<size_t>(os) * p.out_stage_bytes +
-               kSlots * kTileBytes + 3 * 32 * 4 + 8 * ns;
+    // rotate_bulk_kernel's output stages: double-buffered unless single
+    // buffering fits more CTAs per SM (228 KB of shared memory, 1 KB reserved
+    // per CTA)
+    auto total = [&](int os) {
+        return static_cast<size_t>(os) * p.out_stage_bytes + kSlots * kTileBytes + 3 * 32 * 4;
     };
     int best_ctas = 0;
-    p.ns = 0;
-    for (int ns : {3, 2}) {
-        if (kDirect) {  // no input stages (p.ns = 0: the kernel's layout starts at the output stages)
-            for (int os : {2, 1}) {
-                const size_t t = total(0, os);
-                const int ctas = static_cast<int>((228 * 1024) / (t + 1024));
-                if (ctas > best_ctas) { best_ctas = ctas; p.ns = 0; p.os = os; }
-            }
-            break;
-        }
-        for (int os : {2, 1}) {
-            const size_t t = total(ns, os);
-            if (t > 200 * 1024) continue;
-            const int ctas = static_cast<int>((228 * 1024) / (t + 1024));
-            if (ctas > best_ctas) { best_ctas = ctas; p.ns = ns; p.os = os; }
-        }
+    for (int os : {2, 1}) {
+        const int ctas = static_cast<int>((228 * 1024) / (total(os) + 1024));
+        if (ctas > best_ctas) { best_ctas = ctas; p.os = os; }
     }
     if (best_ctas == 0) return -1;
-    const size_t smem = total(p.ns, p.os);
-    if (kDirect && G <= 32) {
+    const size_t smem = total(p.os);
+    if (G <= 32) {
         // one batch per CTA-sized team of half-warps: the team size whose
         // batches fill the most slots, the smallest of equals
         int slots = 16;
@@ -1048,16 +920,6 @@ int check_scale_math(int64_t *bad_scale, int64_t *bad_quant) {
                   std::to_string(got[2]) + ", column division " + std::to_string(got[3]) +
                   " mismatches");
     return 0;
-}
-
-int rot_fault_status(int reset) {
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_rot_fault, sizeof(int)) != cudaSuccess) return -1;
-    if (reset && v) {
-        const int zero = 0;
-        cudaMemcpyToSymbol(g_rot_fault, &zero, sizeof(int));
-    }
-    return v;
 }
 
 }  // namespace xpuint8

@@ -77,8 +77,11 @@ def _signatures():
         "xpuint8_quantize_row_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_colquant_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_fault_status": [i32],
+        "xpuint8_wait_probe": [i64, i32, vp],
         "xpuint8_check_scale_math": [vp, vp],
         "xpuint8_linear_allgather_stream": [vp] * 6 + [i32, i32, vp, vp] + [i64] * 3 + [i32],
+        "xpuint8_linear_allgather_cols_stream": [vp] * 6 + [i32, i64, i64, vp, vp] + [i64] * 3
+                                                + [i32],
         "xpuint8_ipc_alloc": [i64, vp, vp],
         "xpuint8_ipc_open": [vp, vp],
         "xpuint8_ipc_close": [vp],

@@ -209,9 +209,10 @@ def linear_nshard_fused(x, w8_local, w_scale_local, bias_local, out: PeerOutput)
     TMA unit over NVLink), at this rank's columns.  Returns ``out.tensor[:M]``,
     the full ``[M, N]`` output (rows of x beyond ``out.m`` are an error).
 
-    Collective over ``out.group``: every rank calls it with its own weight block
-    (equal blocks, ``N / P`` columns each).  Before the GEMM the ranks wait for
-    each other's readers of the previous output; after it, for each other's
+    Collective over ``out.group``: every rank calls it with its own weight block,
+    the output channels ``col_range(N, P, rank)`` of :func:`shard_weight` (blocks
+    of multiples of 16 columns, equal or not).  Before the GEMM the ranks wait
+    for each other's readers of the previous output; after it, for each other's
     stores.
     """
     from . import ops
@@ -227,8 +228,10 @@ def linear_nshard_fused(x, w8_local, w_scale_local, bias_local, out: PeerOutput)
     reason = ops.unsupported_reason(x2, w8_local, w_scale_local)
     if reason is not None:
         raise TypeError(reason)
-    if n * out.world != out.n_total:
-        raise ValueError(f"{out.world} blocks of {n} columns do not make the output's {out.n_total}")
+    c0, c1 = col_range(out.n_total, out.world, out.rank)
+    if n != c1 - c0:
+        raise ValueError(f"rank {out.rank} holds {n} output channels; its block of the "
+                         f"output's {out.n_total} columns is [{c0}, {c1})")
     if m > out.m:
         raise ValueError(f"{m} rows do not fit the output's {out.m}")
     dev = x2.device
@@ -239,9 +242,9 @@ def linear_nshard_fused(x, w8_local, w_scale_local, bias_local, out: PeerOutput)
     xq = torch.empty((m, k), dtype=torch.int8, device=dev)
     xs = torch.empty((m,), dtype=torch.float32, device=dev)
     _device_barrier(out.group, dev)
-    rc = lib.xpuint8_linear_allgather_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws), _ptr(b),
-                                             out.table, out.world, out.rank, _ptr(xq), _ptr(xs),
-                                             m, n, k, 0)
+    rc = lib.xpuint8_linear_allgather_cols_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws),
+                                                  _ptr(b), out.table, out.world, c0, out.n_total,
+                                                  _ptr(xq), _ptr(xs), m, n, k, 0)
     if rc != 0:
         _err(lib, "linear_nshard_fused")
     _device_barrier(out.group, dev)

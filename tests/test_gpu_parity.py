@@ -3,8 +3,10 @@
 Integer and byte results must be bit-exact (int32 accumulators, int8 codes of
 the pure rotation paths, bf16 outputs of the rotation / dequant paths whose
 fp32 arithmetic the oracle restates operation for operation).  Where a device
-transcendental (erf, tanh, exp) enters, codes may differ by 1 at a rate below
-1e-3 and bf16 outputs by a relative L2 of 1e-2, the north-star tolerance.
+transcendental (erf, tanh, exp) enters, the north-star tolerance applies:
+int8 codes may differ by 1 at a rate below 1e-4 (counted over every code a
+test produces, and printed), bf16 outputs by a relative L2 of 1e-2; and every
+row whose codes match the oracle's exactly must give bit-identical outputs.
 
 Large shapes are checked through size-independent properties: rows are
 independent in every kernel of the forward, so a sample of rows of a full-size
@@ -62,10 +64,22 @@ def rand_i8(shape, seed):
     return torch.randint(-127, 128, shape, generator=g, dtype=torch.int8)
 
 
-def codes_close(got, ref, rate=1e-4):
+#: the north-star bound on int8 codes that differ (by 1) where a device
+#: transcendental enters the activation
+CODE_RATE = 1e-4
+
+
+def code_mismatches(got, ref):
+    """(number of codes that differ, number of codes); every difference must be +-1."""
     d = np.abs(got.astype(np.int16) - ref.astype(np.int16))
-    assert d.max() <= 1, f"max code difference {d.max()}"
-    assert (d > 0).mean() < rate, f"mismatch rate {(d > 0).mean():.2e}"
+    assert d.max(initial=0) <= 1, f"max code difference {d.max()}"
+    return int((d > 0).sum()), int(d.size)
+
+
+def codes_close(got, ref, rate=CODE_RATE, what="codes"):
+    bad, n = code_mismatches(got, ref)
+    print(f"\n{what}: {bad} of {n} codes differ by 1 (rate {bad / max(n, 1):.2e})")
+    assert bad / max(n, 1) < rate, f"mismatch rate {bad / n:.2e}"
 
 
 def scales_close(got, ref, ulps=1):
@@ -150,16 +164,24 @@ def test_quantize_full_c5_every_code():
 
 
 @pytest.mark.parametrize("act", ["gelu_tanh", "swiglu", "situ", "geglu_erf", "gelu_erf"])
-@pytest.mark.parametrize("m,k", [(5, 256), (64, 1280), (33, 4096)])
-def test_quantize_act(act, m, k):
+def test_quantize_act(act):
+    """Each fused input activation over three shapes (edge, C2-like, C5-like
+    rows): codes within +-1 of the oracle's at a rate below 1e-4 of all the
+    codes, and every row whose scale is the oracle's has the oracle's codes
+    wherever its activations round to the same bf16."""
     from xpu_kernels import int8
-    kin = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
-    x = rand_bf16((m, kin), 30 + k, scale=2.0)
-    q, s = int8.quantize_act(x.to(DEV), act)
-    qr, sr = O.convrot_quantize(bits(x), int8.ACTIVATIONS[act])
-    codes_close(bits(q), qr, rate=1e-3)
-    scales_close(bits(s), sr, ulps=2 ** 16)  # a 1-ulp bf16 activation can move the row max
-    assert np.abs(bits(s) / sr - 1).max() < 1e-2
+    bad = total = 0
+    for m, k in [(5, 256), (512, 1280), (65, 4096)]:
+        kin = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
+        x = rand_bf16((m, kin), 30 + k, scale=2.0)
+        q, s = int8.quantize_act(x.to(DEV), act)
+        qr, sr = O.convrot_quantize(bits(x), int8.ACTIVATIONS[act])
+        b, n = code_mismatches(bits(q), qr)
+        bad, total = bad + b, total + n
+        scales_close(bits(s), sr, ulps=2 ** 16)  # a 1-ulp bf16 activation can move the row max
+        assert np.abs(bits(s) / sr - 1).max() < 1e-2
+    print(f"\nquantize_act {act}: {bad} of {total} codes differ by 1 (rate {bad / total:.2e})")
+    assert bad / total < CODE_RATE
 
 
 @pytest.mark.parametrize("n,k", [(16, 256), (300, 1280), (64, 5120)])
@@ -176,18 +198,25 @@ def test_dequant_weight_is_bit_exact(n, k):
 
 
 @pytest.mark.parametrize("act", ["situ", "geglu_erf", "gelu_erf"])
-@pytest.mark.parametrize("m,k", [(7, 256), (64, 1280), (19, 5120)])
-def test_dequant_act_quantize(act, m, k):
+def test_dequant_act_quantize(act):
+    """Dequant + activation + rotate + quantize of an up-projection accumulator
+    over three shapes: codes within +-1 at a rate below 1e-4 of all codes."""
     from xpu_kernels import int8
-    n = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
-    g = torch.Generator().manual_seed(50 + k)
-    acc = torch.randint(-200000, 200000, (m, n), generator=g, dtype=torch.int32)
-    xs = torch.rand(m, generator=g) * 1e-3 + 1e-5
-    ws = torch.rand(n, generator=g) * 1e-3 + 1e-5
-    q, s = int8.dequant_act_quantize(acc.to(DEV), xs.to(DEV), ws.to(DEV), act)
-    qr, sr = O.dequant_act_quantize(bits(acc), bits(xs), bits(ws), int8.ACTIVATIONS[act])
-    codes_close(bits(q), qr, rate=1e-3)
-    assert np.abs(bits(s) / sr - 1).max() < 1e-2
+    bad = total = 0
+    for m, k in [(7, 256), (512, 1280), (19, 5120)]:
+        n = 2 * k if act in int8.PAIRED_ACTIVATIONS else k
+        g = torch.Generator().manual_seed(50 + k)
+        acc = torch.randint(-200000, 200000, (m, n), generator=g, dtype=torch.int32)
+        xs = torch.rand(m, generator=g) * 1e-3 + 1e-5
+        ws = torch.rand(n, generator=g) * 1e-3 + 1e-5
+        q, s = int8.dequant_act_quantize(acc.to(DEV), xs.to(DEV), ws.to(DEV), act)
+        qr, sr = O.dequant_act_quantize(bits(acc), bits(xs), bits(ws), int8.ACTIVATIONS[act])
+        b, nn = code_mismatches(bits(q), qr)
+        bad, total = bad + b, total + nn
+        assert np.abs(bits(s) / sr - 1).max() < 1e-2
+    print(f"\ndequant_act_quantize {act}: {bad} of {total} codes differ by 1 "
+          f"(rate {bad / total:.2e})")
+    assert bad / total < CODE_RATE
 
 
 # ------------------------------------------------------------------------ dequant epilogue
@@ -332,7 +361,12 @@ def test_gemm_geglu_epilogue(m, inner, k):
     d = O.round_bf16((acc.astype(np.float32) * (bits(ws)[None, :] * bits(xs)[:, None]).astype(np.float32)).astype(np.float32))
     ref = O.f32_to_bf16_bits(O.activation(4, d[:, :inner], d[:, inner:]))
     got = bits(y)
-    assert (got != ref).mean() < 1e-3        # erf differs from the oracle's in rare last bits
+    # the device erf differs from the correctly rounded one in rare last bits,
+    # which can move a bf16 rounding: at most 1e-4 of the values
+    diff = int((got != ref).sum())
+    print(f"\nGEGLU epilogue {m}x{inner}x{k}: {diff} of {got.size} bf16 values differ "
+          f"(rate {diff / got.size:.2e})")
+    assert diff / got.size < CODE_RATE
     assert rel_l2(got, ref) < 1e-3
 
 
@@ -477,6 +511,45 @@ def test_linear_dw_int8_matches_the_oracle():
     assert np.array_equal(got, ref)
 
 
+def _ffn_codes(x, up8, up_s, act):
+    """The FFN's intermediate int8 codes on the GPU, step by step through the
+    library (the same kernels the fused entry runs)."""
+    import ctypes  # noqa: F401
+    from xpu_kernels import int8
+    from xpu_kernels.int8 import _lib as L
+    lib = L.load()
+    xq, xs = int8.quantize(x)
+    if act == "geglu_erf":
+        inner = up8.shape[0] // 2
+        y = torch.empty((x.shape[0], inner), dtype=torch.bfloat16, device=DEV)
+        rc = lib.xpuint8_int_mm_geglu_stream(L._stream(y.device), L._ptr(xq), L._ptr(up8), L._ptr(y),
+                                             L._ptr(xs), L._ptr(up_s), x.shape[0], inner, x.shape[1])
+        assert rc == 0, lib.xpuint8_last_error()
+        return int8.quantize(y)
+    acc = int8.int_mm(xq, up8)
+    return int8.dequant_act_quantize(acc, xs, up_s, act)
+
+
+def _check_ffn_rows(x, up8, up_s, dn8, dn_s, dn_b, act, got, rows, ref):
+    """The FFN on `rows` (got: the fused entry's output on those rows; ref: the
+    oracle's): the intermediate codes differ from the oracle's by +-1 at a rate
+    below 1e-4, the bf16 output is within rel-L2 1e-2, and every row whose
+    intermediate codes equal the oracle's gives bit-identical outputs."""
+    from xpu_kernels import int8
+    q2, _ = _ffn_codes(x, up8, up_s, act)
+    q2 = bits(q2)[rows]
+    xq_r, xs_r = O.convrot_quantize(bits(x)[rows])
+    acc_r = O.int_mm(xq_r, bits(up8))
+    q2r, _ = O.dequant_act_quantize(acc_r, xs_r, O._expand(bits(up_s), acc_r.shape[1]),
+                                    int8.ACTIVATIONS[act])
+    codes_close(q2, q2r, what=f"FFN {act} intermediate")
+    same = np.all(q2 == q2r, axis=1)
+    assert rel_l2(got, ref) < 1e-2, rel_l2(got, ref)
+    assert np.array_equal(got[same], ref[same]), "a row with the oracle's codes differs"
+    print(f"FFN {act}: {int(same.sum())} of {len(rows)} rows bit-exact, "
+          f"rel-L2 {rel_l2(got, ref):.2e}")
+
+
 @pytest.mark.parametrize("act", ["geglu_erf", "situ", "gelu_erf"])
 def test_ffn_matches_the_oracle(act):
     from xpu_kernels import int8
@@ -489,7 +562,9 @@ def test_ffn_matches_the_oracle(act):
                         torch.from_numpy(dn8).to(DEV), torch.from_numpy(dn_s).to(DEV), act=act))
     ref = O.ffn(bits(x), up8, up_s, dn8, dn_s, None, int8.ACTIVATIONS[act])
     assert rel_l2(got, ref) < 1e-2
-    assert (got != ref).mean() < 0.05
+    _check_ffn_rows(x.to(DEV), torch.from_numpy(up8).to(DEV), torch.from_numpy(up_s).to(DEV),
+                    torch.from_numpy(dn8).to(DEV), torch.from_numpy(dn_s).to(DEV), None, act,
+                    got, np.arange(m), ref)
 
 
 def test_geglu_ffn_equals_the_unfused_chain():
@@ -507,7 +582,9 @@ def test_geglu_ffn_equals_the_unfused_chain():
     h, gt = d.chunk(2, dim=-1)
     q2, xs2 = int8.quantize(h * torch.nn.functional.gelu(gt))
     chain = int8.dequant(int8.int_mm(q2, dn8), xs2, dn_s)
-    assert (fused.view(torch.int16) != chain.view(torch.int16)).float().mean().item() < 1e-3
+    diff = int((fused.view(torch.int16) != chain.view(torch.int16)).sum().item())
+    print(f"\nfused GEGLU FFN vs the unfused chain: {diff} of {fused.numel()} values differ")
+    assert diff / fused.numel() < CODE_RATE
 
 
 def test_selftest_passes():
@@ -541,3 +618,96 @@ def test_full_size_linear_on_sampled_rows(cfg):
     rel = torch.linalg.norm((y.float() - (x.float() @ w.float().t()))) / \
         torch.linalg.norm(x.float() @ w.float().t())
     assert rel.item() < 2e-2
+
+
+def test_full_size_ffn_c3_on_sampled_rows():
+    """Config C3 at full size: x [2048, 1280] through the GEGLU FFN, W1 [10240,
+    1280] (hidden | gate halves of 5120) and W2 [1280, 5120], prepared with
+    prepare_weight.  Rows are independent, so 24 sampled rows are checked
+    against the oracle: intermediate codes at a +-1 rate below 1e-4, output
+    rel-L2 below 1e-2, rows with the oracle's codes bit-exact."""
+    from xpu_kernels import int8
+    m, k, inner = 2048, 1280, 5120
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+    w1 = (torch.randn(2 * inner, k, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    w2 = (torch.randn(k, inner, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    up8, up_s = int8.prepare_weight(w1)
+    dn8, dn_s = int8.prepare_weight(w2)
+    y = int8.ffn(x, up8, up_s, dn8, dn_s, act="geglu_erf")
+    rows = torch.randperm(m, generator=g)[:24].sort().values.numpy()
+    ref = O.ffn(bits(x)[rows], bits(up8), bits(up_s), bits(dn8), bits(dn_s), None, 4)
+    _check_ffn_rows(x, up8, up_s, dn8, dn_s, None, "geglu_erf", bits(y)[rows], rows, ref)
+    # against the unquantized bf16 FFN (reported: the quantization error of the path)
+    h, gt = (x.float() @ w1.float().t()).chunk(2, dim=-1)
+    dense = (h * torch.nn.functional.gelu(gt)) @ w2.float().t()
+    rel = (torch.linalg.norm(y.float() - dense) / torch.linalg.norm(dense)).item()
+    print(f"C3 FFN vs the unquantized fp32 FFN: rel-L2 {rel:.3e}")
+    assert rel < 5e-2
+
+
+def test_full_size_backward_c4():
+    """Config C4 at full size (x [4096, 1280], W [5120, 1280], dy [4096, 5120]
+    ~ N(0, 1e-3)): linear_dx_int8 bit-exact on 24 sampled rows (rows are
+    independent) and linear_dw_int8 bit-exact on 24 sampled output channels (the
+    column quantizer scales each column of dy on its own, so a subset of dy's
+    columns gives exactly those rows of dW).  The relative L2 error of both
+    against the unquantized fp32 autograd of the linear is printed."""
+    from xpu_kernels import int8
+    m, k, n = 4096, 1280, 5120
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    dy = (torch.randn(m, n, generator=g) * 1e-3).to(torch.bfloat16).to(DEV)
+    w8, ws = int8.prepare_weight(w)
+    dx = int8.linear_dx_int8(dy, w8, ws)
+    rows = torch.randperm(m, generator=g)[:24].sort().values.numpy()
+    assert np.array_equal(bits(dx)[rows], O.linear_dx_int8(bits(dy)[rows], bits(w8), bits(ws)))
+    xq, xs = int8.quantize(x)
+    dw = int8.linear_dw_int8(dy, xq, xs)
+    cols = torch.randperm(n, generator=g)[:24].sort().values.numpy()
+    ref_dw = O.linear_dw_int8(bits(dy)[:, cols], bits(xq), bits(xs))
+    assert np.array_equal(bits(dw)[cols], ref_dw)
+    # the torch autograd of the unquantized linear y = x W^T
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    (xf @ wf.t()).backward(dy.float())
+    rdx = (torch.linalg.norm(dx.float() - xf.grad) / torch.linalg.norm(xf.grad)).item()
+    rdw = (torch.linalg.norm(dw.float() - wf.grad) / torch.linalg.norm(wf.grad)).item()
+    print(f"\nC4 backward vs the unquantized fp32 autograd: dx rel-L2 {rdx:.3e}, "
+          f"dW rel-L2 {rdw:.3e}")
+    assert rdx < 5e-2 and rdw < 5e-2
+
+
+@pytest.mark.parametrize("m,widths,k", [(1000, (1040, 1024), 1280), (77, (48, 32, 64), 512)])
+def test_allgather_ragged_blocks_on_one_gpu(m, widths, k):
+    """The all-gather linear with column blocks of unequal widths (the
+    explicit-offset entry): each 'rank' stores its block at its own offset of
+    every buffer; every buffer equals the linear of the whole weight."""
+    import ctypes
+    from xpu_kernels import int8
+    from xpu_kernels.int8 import _lib as L
+    lib = L.load()
+    n = sum(widths)
+    _, w8n, wsn = _prep(n, k, 190 + k)
+    w8, ws = torch.from_numpy(w8n).to(DEV), torch.from_numpy(wsn).to(DEV)
+    x = rand_bf16((m, k), 191 + m, outliers=4).to(DEV)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(n)) * 0.01).to(DEV)
+    full = int8.linear(x, w8, ws, bias)
+    nr = len(widths)
+    outs = [torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(nr)]
+    table = (ctypes.c_void_p * nr)(*[o.data_ptr() for o in outs])
+    xq = torch.empty(m, k, dtype=torch.int8, device=DEV)
+    xs = torch.empty(m, dtype=torch.float32, device=DEV)
+    c0 = 0
+    for wdt in widths:
+        sl = slice(c0, c0 + wdt)
+        w8r, wsr, br = w8[sl].contiguous(), ws[sl].contiguous(), bias[sl].contiguous()
+        rc = lib.xpuint8_linear_allgather_cols_stream(
+            L._stream(torch.device(DEV)), L._ptr(x), L._ptr(w8r), L._ptr(wsr), L._ptr(br), table,
+            nr, c0, n, L._ptr(xq), L._ptr(xs), m, wdt, k, 0)
+        assert rc == 0, lib.xpuint8_last_error()
+        c0 += wdt
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o.view(torch.int16), full.view(torch.int16))

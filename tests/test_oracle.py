@@ -179,3 +179,30 @@ def test_int_mm_is_exact():
     b = rng.integers(-127, 128, (48, 160), dtype=np.int8)
     ref = a.astype(np.int64) @ b.astype(np.int64).T
     assert np.array_equal(O.int_mm(a, b), ref.astype(np.int32))
+
+
+def test_torch_cpu_restatement_of_convrot_linear_as_shipped(G):
+    """oracle/convrot_torch_cpu.py (the benchmark's reference arm) gives the
+    shipped reference/convrot_linear.py's bits, and with the Hadamard the numpy
+    restatement's."""
+    import torch
+    from oracle import convrot_torch_cpu as T
+
+    def t16(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+
+    x, w8 = t16(G["cl_x"]), torch.from_numpy(G["cl_w8"])
+    ws, b = torch.from_numpy(G["cl_ws"]), t16(G["cl_bias"])
+    y = T.convrot_int8_linear_cpu(x, w8, ws, b, rotation="identity")
+    assert np.array_equal(y.view(torch.int16).numpy().view(np.uint16), G["cl_out"])
+    y0 = T.convrot_int8_linear_cpu(x, w8, ws, None, rotation="identity")
+    assert np.array_equal(y0.view(torch.int16).numpy().view(np.uint16), G["cl_out_nobias"])
+    yh = T.convrot_int8_linear_cpu(x, w8, ws, b, rotation="hadamard")
+    ref = O.convrot_linear_reference(G["cl_x"], G["cl_w8"], G["cl_ws"],
+                                     O.bf16_bits_to_f32(G["cl_bias"]), rotation="hadamard")
+    got = yh.view(torch.int16).numpy().view(np.uint16)
+    # the bf16 matmul's accumulation order may differ from float64-then-round in
+    # rare last bits of x_rot; the outputs agree to a bf16 ulp at most there
+    d = np.abs(O.bf16_bits_to_f32(got).astype(np.float64) - O.bf16_bits_to_f32(ref))
+    assert (got != ref).mean() < 0.02 and d.max() <= 0.02 * np.abs(O.bf16_bits_to_f32(ref)).max()
+    assert np.array_equal(T.hadamard_bf16().float().numpy(), O.hadamard_matrix().astype(np.float32))

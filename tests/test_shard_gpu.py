@@ -89,25 +89,29 @@ def _fused_worker(rank, world, port, outdir):
     import xpu_kernels
     from xpu_kernels.int8 import shard
     g = torch.Generator(device=dev).manual_seed(21)
-    k, n = 1280, 2048
-    w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    w8, ws = xpu_kernels.prepare_weight(w)
-    bias = torch.randn(n, generator=g, device=dev) * 0.01
-    w8l, wsl, bl = shard.shard_weight(w8, ws, world, rank, bias)
-    out = shard.PeerOutput(1000, n)
+    k = 1280
     oks = []
-    # two calls in a row (the second overwrites the first's output in every
-    # rank's buffer), a ragged row count, then fewer rows than the buffer holds
-    for m, seed in ((1000, 1), (1000, 2), (333, 3)):
-        gx = torch.Generator(device=dev).manual_seed(seed)
-        x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
-        full = xpu_kernels.linear(x, w8, ws, bias)
-        y = shard.linear_nshard_fused(x, w8l, wsl, bl, out)
-        torch.cuda.synchronize()
-        oks.append(int(torch.equal(y.view(torch.int16), full.view(torch.int16))))
+    # n = 2048 splits into equal blocks at 2, 4 and 8 ranks and into ragged ones
+    # (e.g. 688/688/672) at 3, 5, 6 and 7; n = 2064 (129 blocks of 16) is ragged
+    # at every rank count
+    for n in (2048, 2064):
+        w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w8, ws = xpu_kernels.prepare_weight(w)
+        bias = torch.randn(n, generator=g, device=dev) * 0.01
+        w8l, wsl, bl = shard.shard_weight(w8, ws, world, rank, bias)
+        out = shard.PeerOutput(1000, n)
+        # two calls in a row (the second overwrites the first's output in every
+        # rank's buffer), a ragged row count, then fewer rows than the buffer holds
+        for m, seed in ((1000, 1), (1000, 2), (333, 3)):
+            gx = torch.Generator(device=dev).manual_seed(seed)
+            x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
+            full = xpu_kernels.linear(x, w8, ws, bias)
+            y = shard.linear_nshard_fused(x, w8l, wsl, bl, out)
+            torch.cuda.synchronize()
+            oks.append(int(torch.equal(y.view(torch.int16), full.view(torch.int16))))
+        out.close()
     from xpu_kernels.int8 import _lib as L
     oks.append(int(L.load().xpuint8_fault_status(1) == 0))
-    out.close()
     with open(os.path.join(outdir, f"f{rank}.txt"), "w") as f:
         f.write(" ".join(map(str, oks)))
     dist.barrier()
@@ -121,4 +125,4 @@ def test_fused_allgather_linear_on_all_gpus(tmp_path):
     while not ctx.join(timeout=300):
         pass
     for r in range(world):
-        assert (tmp_path / f"f{r}.txt").read_text() == "1 1 1 1"
+        assert (tmp_path / f"f{r}.txt").read_text() == "1 1 1 1 1 1 1"
