@@ -138,6 +138,19 @@ int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
                           const float *w_scale, const float *bias, void *out, int8_t *xq,
                           float *xs, int64_t M, int64_t N, int64_t K, int32_t activation);
 
+/* The INT8 linear against a weight of `nparts` concatenated projections
+ * (q, k, v: w8 [nparts*N, K] = cat(Wq, Wk, Wv), w_scale [nparts*N], bias
+ * [nparts*N] or NULL) in one GEMM whose drain writes part i's columns straight
+ * into outs[i] (bf16 [M, N] each) -- no int32 [M, nparts*N] accumulator in
+ * HBM.  Bit-identical to linear_acc + xpuint8_dequant_epilogue_slice per part.
+ * xq [M,K], xs [M] are caller scratch.  N % 32 == 0, nparts <= 8.  Replaces
+ * the reference's fused qkv pattern, python/xpu_kernels/int8/ops.py:500-525
+ * (linear_acc, dequant_slice) as used at int8/selftest.py:67-72. */
+int xpuint8_linear_split_stream(const void *stream, const void *x, const int8_t *w8,
+                                const float *w_scale, const float *bias, void *const *outs,
+                                int32_t nparts, int8_t *xq, float *xs, int64_t M, int64_t N,
+                                int64_t K, int32_t activation);
+
 /* The fused FFN down(act(up(x))) (ops.py:649-719) in one C call; activation 3
  * situ, 4 GEGLU (fused into the up-projection's epilogue), 5 GELU-erf.
  * `workspace` holds xpuint8_ffn_workspace_bytes(M, K, inner, activation)
@@ -155,6 +168,31 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
  * quantize_row_torch (ops.py:320-330).  K % 8 == 0. */
 int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *col_scale,
                                 int8_t *q, float *scale, int64_t M, int64_t K);
+
+/* dL/dx of the INT8 linear with the weight kept in int8, in one C call:
+ * dy bf16 [M,N], w8 int8 [N,K] and w_scale fp32 [N] (the forward's prepared
+ * weight) -> dx bf16 [M,K].  The column-scaled row quantizer, the int8 GEMM
+ * reading w8 as stored with the row-scale epilogue, and the rotation undone
+ * along K, launched back to back (the GEMM with programmatic serialization).
+ * `workspace` holds xpuint8_linear_dx_int8_workspace_bytes(M, N, K) bytes.
+ * K % 256 == 0, N % 16 == 0.  Replaces the chain of
+ * python/xpu_kernels/int8/ops.py:353-377 (linear_dx_int8). */
+int64_t xpuint8_linear_dx_int8_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int xpuint8_linear_dx_int8_stream(const void *stream, const void *dy, const int8_t *w8,
+                                  const float *w_scale, void *dx, void *workspace, int64_t M,
+                                  int64_t N, int64_t K);
+
+/* dL/dW with both GEMM operands int8, in one C call: dy bf16 [M,N], the
+ * forward's rotated int8 activation xq [M,K] and its row scales x_scale [M]
+ * -> dW bf16 [N,K] = rotate_K(bf16(colquant(dy*xs)^T @ xq * tg)).  The column
+ * quantizer, the int8 GEMM with both operands MN-major, and the rotation.
+ * `workspace` holds xpuint8_linear_dw_int8_workspace_bytes(M, N, K) bytes.
+ * K % 256 == 0, N % 16 == 0.  No counterpart in the reference, whose weight
+ * gradient is the bf16 matmul of python/xpu_kernels/int8/ops.py:207-238. */
+int64_t xpuint8_linear_dw_int8_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int xpuint8_linear_dw_int8_stream(const void *stream, const void *dy, const int8_t *xq,
+                                  const float *x_scale, void *dw, void *workspace, int64_t M,
+                                  int64_t N, int64_t K);
 
 /* Column quantization of g = dy[m,n] * x_scale[m] over m, for the int8 weight
  * gradient: gq int8 [M,N], tg fp32 [N].  N % 16 == 0. */

@@ -422,6 +422,39 @@ int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
                          K, 0, N, true);
 }
 
+int xpuint8_linear_split_stream(const void *stream, const void *x, const int8_t *w8,
+                                const float *w_scale, const float *bias, void *const *outs,
+                                int32_t nparts, int8_t *xq, float *xs, int64_t M, int64_t N,
+                                int64_t K, int32_t activation) {
+    if (N <= 0 || N % 32 != 0) {
+        set_error("linear_split: each part's width N must be a positive multiple of 32");
+        return 2;
+    }
+    if (!outs || nparts < 1 || nparts > 8) {
+        set_error("linear_split: 1 <= nparts <= 8 and an output table are required");
+        return 2;
+    }
+    for (int i = 0; i < nparts; ++i) {
+        if (!outs[i] || !aligned16(outs[i])) {
+            set_error("linear_split: every output buffer needs a 16-byte aligned base");
+            return 2;
+        }
+    }
+    if (!w8 || !w_scale || !aligned16(w8) || !aligned16(w_scale) || (bias && !aligned16(bias))) {
+        set_error("linear_split: w8, w_scale (and bias) must be non-null and 16-byte aligned");
+        return 2;
+    }
+    if (int rc = convrot_quantize(as_stream(stream), x, xq, xs, M, K, activation)) return rc;
+    GemmCall c;
+    c.epilogue = kEpiDequantBf16;
+    c.a = xq; c.b = w8; c.lda = K; c.ldb = K;
+    c.outs = outs; c.nout = nparts; c.ldo = N; c.split_n = N;
+    c.row_scale = xs; c.col_scale = w_scale; c.bias = bias;
+    c.M = M; c.N = static_cast<int64_t>(nparts) * N; c.K = K;
+    c.b_early = true;  // the quantizer above is the kernel just before
+    return launch_gemm(as_stream(stream), c);
+}
+
 int64_t xpuint8_ffn_workspace_bytes(int64_t M, int64_t K, int64_t inner, int32_t activation) {
     if (M <= 0 || K <= 0 || inner <= 0) return -1;
     return static_cast<int64_t>(ffn_layout(M, K, inner, activation).total);
@@ -469,6 +502,106 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
     }
     return int_mm_common(s, kEpiDequantBf16, q2, down_w8, out, xs2, down_scale, down_bias, M, K,
                          inner, 0, K, true);
+}
+
+// ------------------------------------------------------------ fused backward
+namespace {
+struct DxLayout {
+    size_t q, a, dxr, total;
+};
+DxLayout dx_layout(int64_t M, int64_t N, int64_t K) {
+    DxLayout L{};
+    size_t off = 0;
+    L.q = off; off += align256(static_cast<size_t>(M) * N);       // int8 row-quantized dy
+    L.a = off; off += align256(static_cast<size_t>(M) * 4);       // its row scales
+    L.dxr = off; off += align256(static_cast<size_t>(M) * K * 2);  // dx before the rotation
+    L.total = off;
+    return L;
+}
+struct DwLayout {
+    size_t gq, tg, dwr, total;
+};
+DwLayout dw_layout(int64_t M, int64_t N, int64_t K) {
+    DwLayout L{};
+    size_t off = 0;
+    L.gq = off; off += align256(static_cast<size_t>(M) * N);       // column-quantized dy * xs
+    L.tg = off; off += align256(static_cast<size_t>(N) * 4);       // its column scales
+    L.dwr = off; off += align256(static_cast<size_t>(N) * K * 2);  // dW before the rotation
+    L.total = off;
+    return L;
+}
+int check_workspace(const void *ws) {
+    if (!ws || !aligned16(ws)) {
+        set_error("the workspace must be a 16-byte aligned buffer");
+        return 2;
+    }
+    return 0;
+}
+}  // namespace
+
+int64_t xpuint8_linear_dx_int8_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return -1;
+    return static_cast<int64_t>(dx_layout(M, N, K).total);
+}
+
+int xpuint8_linear_dx_int8_stream(const void *stream, const void *dy, const int8_t *w8,
+                                  const float *w_scale, void *dx, void *workspace, int64_t M,
+                                  int64_t N, int64_t K) {
+    cudaStream_t s = as_stream(stream);
+    if (int rc = check_mk(M, K)) return rc;
+    if (N <= 0 || N % 16 != 0) {
+        set_error("linear_dx_int8: N must be a positive multiple of 16");
+        return 2;
+    }
+    if (int rc = check_ptrs({dy, w8, w_scale, dx})) return rc;
+    if (int rc = check_workspace(workspace)) return rc;
+    const DxLayout L = dx_layout(M, N, K);
+    char *ws = static_cast<char *>(workspace);
+    int8_t *q = reinterpret_cast<int8_t *>(ws + L.q);
+    float *a = reinterpret_cast<float *>(ws + L.a);
+    void *dxr = ws + L.dxr;
+    // d = bf16(dy * bf16(w_scale)) row-quantized in one pass
+    if (int rc = launch_quantize_row(s, dy, w_scale, q, a, M, N)) return rc;
+    // dxr = bf16(float(q @ w8) * a[m]): w8 [N, K] read as stored (MN-major B)
+    if (int rc = int_mm_common(s, kEpiDequantBf16, q, w8, dxr, a, nullptr, nullptr, M, K, N, 1, K,
+                               true))
+        return rc;
+    // the rotation undone along K
+    return launch_rotate_rows(s, 2, 0, dxr, nullptr, nullptr, dx, nullptr, M, K);
+}
+
+int64_t xpuint8_linear_dw_int8_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return -1;
+    return static_cast<int64_t>(dw_layout(M, N, K).total);
+}
+
+int xpuint8_linear_dw_int8_stream(const void *stream, const void *dy, const int8_t *xq,
+                                  const float *x_scale, void *dw, void *workspace, int64_t M,
+                                  int64_t N, int64_t K) {
+    cudaStream_t s = as_stream(stream);
+    if (int rc = check_mk(M, K)) return rc;
+    if (N <= 0 || N % 16 != 0) {
+        set_error("linear_dw_int8: N must be a positive multiple of 16");
+        return 2;
+    }
+    if (int rc = check_ptrs({dy, xq, dw})) return rc;
+    if (!x_scale) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    if (int rc = check_workspace(workspace)) return rc;
+    const DwLayout L = dw_layout(M, N, K);
+    char *ws = static_cast<char *>(workspace);
+    int8_t *gq = reinterpret_cast<int8_t *>(ws + L.gq);
+    float *tg = reinterpret_cast<float *>(ws + L.tg);
+    void *dwr = ws + L.dwr;
+    // g = dy * xs[m] quantized per column n (over the tokens m)
+    if (int rc = launch_colquant(s, dy, x_scale, gq, tg, M, N)) return rc;
+    // dwr [N, K] = bf16(float(gq^T @ xq) * tg[n]): both operands MN-major
+    if (int rc = int_mm_common(s, kEpiDequantBf16, gq, xq, dwr, tg, nullptr, nullptr, N, K, M, 2, K,
+                               true))
+        return rc;
+    return launch_rotate_rows(s, 2, 0, dwr, nullptr, nullptr, dw, nullptr, N, K);
 }
 
 int xpuint8_quantize_row_stream(const void *stream, const void *x, const float *col_scale,

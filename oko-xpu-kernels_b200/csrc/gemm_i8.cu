@@ -15,6 +15,8 @@
 //   geglu   B holds [hidden | gate] rows; a CTA loads hidden rows [n, n+128)
 //           and gate rows [N+n, N+n+128) into one 256-wide B tile, and writes
 //           y = bf16(h * bf16(gelu_erf(g))) with h, g the bf16-rounded dequants
+//   split   the dequant epilogue with the output's columns cut into parts that
+//           land in separate buffers (q, k, v of one projection GEMM)
 //
 // Structure: persistent CTA pairs (clusters of 2 on neighbouring SMs, one CTA
 // per SM, 320 threads each) walk 256 x bn output tiles; the pair's MMAs are
@@ -76,12 +78,17 @@ struct GemmArgs {
     // num_m counts 256-row pair tiles
     int b_early;  // B, the column scales and the bias may be read before the
                   // wait for the previous kernel (it does not write them)
+    int split_n;  // > 0: output column n goes to destination n / split_n, column
+                  // n % split_n (the split projection: q, k, v from one GEMM)
 };
 
-// The output's tensor maps: one per destination.  Every output tile is
+// The output's tensor maps: one per destination.  Either every output tile is
 // stored to each of them (the N-sharded linear's all-gather: this rank's
 // column block into every rank's output, peers' buffers mapped by CUDA IPC
-// and written over NVLink by the TMA unit, tile by tile as the tiles finish).
+// and written over NVLink by the TMA unit, tile by tile as the tiles finish),
+// or (split_n > 0) the output's columns are cut into consecutive parts of
+// split_n columns and each part goes to its own destination (the q, k and v
+// projections from one GEMM over the concatenated weight).
 constexpr int kMaxOut = 8;
 struct OutMaps {
     CUtensorMap m[kMaxOut];
@@ -163,16 +170,24 @@ __device__ __forceinline__ void stage_bf16_32(uint32_t buf, int lane, const floa
                      cvt_bf16x2(v[8 * c + 6], v[8 * c + 7]));
 }
 
-// hand a filled buffer to the TMA unit (one lane: a store per destination,
-// one bulk group), then flip buffers
-__device__ __forceinline__ void stage_flush(const OutMaps &om, uint32_t buf, int lane, int x, int y) {
+// hand a filled buffer to the TMA unit (one lane: a store per destination, or
+// to the one destination of its part when split_n > 0; one bulk group), then
+// flip buffers.  A split part is a multiple of the chunk width, so a chunk
+// never straddles two parts.
+__device__ __forceinline__ void stage_flush(const OutMaps &om, uint32_t buf, int lane, int x, int y,
+                                            int split_n) {
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(&om.m[0], buf, x, y);
+        if (split_n > 0) {
+            const int part = x / split_n;
+            tma_store_2d(&om.m[part], buf, x - part * split_n, y);
+        } else {
+            tma_store_2d(&om.m[0], buf, x, y);
 #pragma unroll
-        for (int i = 1; i < kMaxOut; ++i)
-            if (i < om.n) tma_store_2d(&om.m[i], buf, x, y);
+            for (int i = 1; i < kMaxOut; ++i)
+                if (i < om.n) tma_store_2d(&om.m[i], buf, x, y);
+        }
         bulk_commit();
     }
 }
@@ -264,7 +279,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             tmem_wait_ld(r1);
             dequant32(r1, s_ws + c + 32, s_b + c + 32, xs2, bias, v);
             stage_bf16_32_wide(buf, lane, 1, v);
-            stage_flush(tmOut, buf, lane, n0 + c, y);
+            stage_flush(tmOut, buf, lane, n0 + c, y, a.split_n);
             bsel ^= 1;
         }
     } else {
@@ -283,7 +298,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
                 for (int q = 0; q < 4; ++q)
                     st_shared_v4(stage_chunk_addr(buf, lane, q), r[16 * h + 4 * q],
                                  r[16 * h + 4 * q + 1], r[16 * h + 4 * q + 2], r[16 * h + 4 * q + 3]);
-                stage_flush(tmOut, buf, lane, n0 + c + 16 * h, y);
+                stage_flush(tmOut, buf, lane, n0 + c + 16 * h, y, a.split_n);
                 bsel ^= 1;
             }
         } else {
@@ -301,7 +316,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             stage_reserve(lane);
             const uint32_t buf = bufs + bsel * kStageBytes;
             stage_bf16_32(buf, lane, v);
-            stage_flush(tmOut, buf, lane, n0 + c, y);
+            stage_flush(tmOut, buf, lane, n0 + c, y, a.split_n);
             bsel ^= 1;
         }
     }
@@ -709,6 +724,15 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("the GEGLU epilogue needs K-major operands");
         return 2;
     }
+    if (c.split_n > 0) {
+        // the split projection: N / split_n parts, each its own [M, split_n] output
+        if (c.epilogue != kEpiDequantBf16 || c.a_mn || c.b_mn || !c.outs ||
+            c.split_n % 32 != 0 || c.N % c.split_n != 0 || c.nout != c.N / c.split_n) {
+            set_error("split output: the dequant epilogue with K-major operands, parts of a "
+                      "multiple of 32 columns, one output buffer per part");
+            return 2;
+        }
+    }
     const uintptr_t oa = reinterpret_cast<uintptr_t>(c.outs ? c.outs[0] : c.out);
     if ((oa & 15u) || (c.ldo % 8)) {
         set_error("the output needs a 16-byte aligned base and a row stride multiple of 8");
@@ -786,7 +810,8 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
                           CU_TENSOR_MAP_SWIZZLE_128B))
                 return 2;
         } else {
-            if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+            const int64_t cols = c.split_n > 0 ? c.split_n : c.N;
+            if (!make_map(&mo.m[i], base, cols, c.M, c.ldo * 2, 32, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                           CU_TENSOR_MAP_SWIZZLE_64B))
                 return 2;
         }
@@ -796,6 +821,7 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
     a.row_scale = c.row_scale; a.col_scale = c.col_scale; a.bias = c.bias;
     a.M = static_cast<int>(c.M); a.N = static_cast<int>(c.N); a.K = static_cast<int>(c.K);
     a.b_early = c.b_early ? 1 : 0;
+    a.split_n = c.split_n > 0 ? static_cast<int>(c.split_n) : 0;
     a.num_m = static_cast<int>((c.M + 2 * BM - 1) / (2 * BM));
     a.bn = geglu ? 128 : bn;
     a.num_n = static_cast<int>((c.N + a.bn - 1) / a.bn);

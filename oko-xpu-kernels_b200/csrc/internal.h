@@ -54,6 +54,9 @@ struct GemmCall {
     int64_t ldo = 0;
     void *const *outs = nullptr;  // instead of out: nout destinations, each tile stored to all
     int nout = 0;
+    // > 0 (with outs): the output's columns in consecutive parts of split_n,
+    // part i stored to outs[i] as its own [M, split_n] (row stride ldo)
+    int64_t split_n = 0;
     const float *row_scale = nullptr;  // [M]  (x_scale)
     const float *col_scale = nullptr;  // [N]  (w_scale) or null = 1; GEGLU: [2N]
     const float *bias = nullptr;       // [N]  or null

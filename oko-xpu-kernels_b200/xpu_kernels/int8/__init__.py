@@ -39,6 +39,7 @@ from .ops import (
     int_mm,
     linear,
     linear_acc,
+    linear_split,
     linear_dw,
     linear_dw_int8,
     linear_dx,
@@ -58,7 +59,7 @@ __all__ = [
     "ACTIVATIONS", "Int8Linear", "PAIRED_ACTIVATIONS", "TrainableInt8Linear", "available",
     "dequant", "dequant_act_quantize", "dequant_slice", "dequant_weight",
     "dequant_weight_torch", "device_name", "expand_scale", "ffn", "ffn_situ", "int8_linear",
-    "int_mm", "linear", "linear_acc", "linear_dw", "linear_dw_int8", "linear_dx",
+    "int_mm", "linear", "linear_acc", "linear_split", "linear_dw", "linear_dw_int8", "linear_dx",
     "linear_dx_int8", "load", "prepare_weight", "prepare_weight_fused", "quantize",
     "quantize_act", "quantize_row", "quantize_row_torch", "rotate", "selftest",
     "unsupported_reason",

@@ -72,10 +72,15 @@ def _signatures():
         "xpuint8_int_mm_dequant_stream": [vp] * 7 + [i64] * 3 + [i32, i64],
         "xpuint8_int_mm_geglu_stream": [vp] * 6 + [i64] * 3,
         "xpuint8_linear_stream": [vp] * 8 + [i64] * 3 + [i32],
+        "xpuint8_linear_split_stream": [vp] * 6 + [i32, vp, vp] + [i64] * 3 + [i32],
         "xpuint8_ffn_workspace_bytes": [i64, i64, i64, i32],
         "xpuint8_ffn_stream": [vp] * 9 + [i64] * 3 + [i32],
         "xpuint8_quantize_row_stream": [vp] * 5 + [i64] * 2,
         "xpuint8_colquant_stream": [vp] * 5 + [i64] * 2,
+        "xpuint8_linear_dx_int8_workspace_bytes": [i64] * 3,
+        "xpuint8_linear_dx_int8_stream": [vp] * 6 + [i64] * 3,
+        "xpuint8_linear_dw_int8_workspace_bytes": [i64] * 3,
+        "xpuint8_linear_dw_int8_stream": [vp] * 6 + [i64] * 3,
         "xpuint8_fault_status": [i32],
         "xpuint8_wait_probe": [i64, i32, vp],
         "xpuint8_check_scale_math": [vp, vp],
@@ -96,7 +101,7 @@ def _bind(lib):
     for name, args in _signatures().items():
         fn = getattr(lib, name)
         fn.argtypes = args
-        fn.restype = ctypes.c_int64 if name == "xpuint8_ffn_workspace_bytes" else ctypes.c_int
+        fn.restype = ctypes.c_int64 if name.endswith("_workspace_bytes") else ctypes.c_int
 
 
 def load():

@@ -220,19 +220,17 @@ def linear_dw_int8(dy, xq, x_scale):
     if xq2.dtype != torch.int8:
         raise TypeError("xq must be the int8 activation of the forward")
     xs = expand_scale(x_scale.reshape(-1), m, dy.device)
-    gq = torch.empty((m, n), dtype=torch.int8, device=dy.device)
-    tg = torch.empty((n,), dtype=torch.float32, device=dy.device)
-    s = _stream(dy.device)
-    rc = lib.xpuint8_colquant_stream(s, _ptr(dy2), _ptr(xs), _ptr(gq), _ptr(tg), m, n)
+    # one C call: column quantizer -> int8 GEMM (both operands MN-major) -> rotation
+    ws_bytes = lib.xpuint8_linear_dw_int8_workspace_bytes(m, n, k)
+    if ws_bytes < 0:
+        raise ValueError(f"linear_dw_int8: bad sizes M={m}, N={n}, K={k}")
+    work = torch.empty((ws_bytes,), dtype=torch.uint8, device=dy.device)
+    dw = torch.empty((n, k), dtype=torch.bfloat16, device=dy.device)
+    rc = lib.xpuint8_linear_dw_int8_stream(_stream(dy.device), _ptr(dy2), _ptr(xq2), _ptr(xs),
+                                           _ptr(dw), _ptr(work), m, n, k)
     if rc != 0:
-        _err(lib, "linear_dw_int8 (column quantizer)")
-    dwr = torch.empty((n, k), dtype=torch.bfloat16, device=dy.device)
-    # layout 2: a = gq [M, N] read as [K=M, M'=N], b = xq [M, K] read as [K=M, N'=K]
-    rc = lib.xpuint8_int_mm_dequant_stream(s, _ptr(gq), _ptr(xq2), _ptr(dwr), _ptr(tg), None,
-                                           None, n, k, m, 2, k)
-    if rc != 0:
-        _err(lib, "linear_dw_int8 (GEMM)")
-    return rotate(dwr)
+        _err(lib, "linear_dw_int8")
+    return dw
 
 
 class _Int8LinearFn(torch.autograd.Function):
@@ -324,17 +322,24 @@ def linear_dx_int8(dy, w8, w_scale):
     """
     lib = _lib()
     d2 = dy.to(torch.bfloat16).reshape(-1, dy.shape[-1])
+    if not d2.is_contiguous():
+        d2 = d2.contiguous()
     n, k = w8.shape
     if d2.shape[1] != n:
         raise ValueError(f"dy has {d2.shape[1]} columns but w8 has {n} rows")
-    q, a = quantize_row(d2, col_scale=w_scale)
-    m = q.shape[0]
-    dxr = torch.empty((m, k), dtype=torch.bfloat16, device=dy.device)
-    rc = lib.xpuint8_int_mm_dequant_stream(_stream(dy.device), _ptr(q), _ptr(w8.contiguous()),
-                                           _ptr(dxr), _ptr(a), None, None, m, k, n, 1, k)
+    m = d2.shape[0]
+    ws = expand_scale(w_scale, n, dy.device)
+    # one C call: column-scaled row quantizer -> int8 GEMM -> rotation
+    ws_bytes = lib.xpuint8_linear_dx_int8_workspace_bytes(m, n, k)
+    if ws_bytes < 0:
+        raise ValueError(f"linear_dx_int8: bad sizes M={m}, N={n}, K={k}")
+    work = torch.empty((ws_bytes,), dtype=torch.uint8, device=dy.device)
+    dx = torch.empty((m, k), dtype=torch.bfloat16, device=dy.device)
+    rc = lib.xpuint8_linear_dx_int8_stream(_stream(dy.device), _ptr(d2), _ptr(w8.contiguous()),
+                                           _ptr(ws), _ptr(dx), _ptr(work), m, n, k)
     if rc != 0:
         _err(lib, "linear_dx_int8")
-    return rotate(dxr).reshape(*dy.shape[:-1], k)
+    return dx.reshape(*dy.shape[:-1], k)
 
 
 def expand_scale(scale, n, device=None):
@@ -588,6 +593,51 @@ def linear(x, w8, w_scale, bias=None, act: Optional[str] = None, residual=None,
         out = torch.addcmul(residual, out, residual_scale)
     out = out.reshape(*x.shape[:-1], n)
     return out if input_dtype == torch.bfloat16 else out.to(dtype=input_dtype)
+
+
+def linear_split(x, w8, w_scale, bias=None, parts: int = 3, act: Optional[str] = None):
+    """The INT8 linear against ``parts`` concatenated projections, one output
+    per projection: ``(y_0, .., y_{parts-1})``, each bf16 [.., N] with
+    ``N = w8.shape[0] // parts``.
+
+    The fused qkv projection: ``w8 = cat([Wq8, Wk8, Wv8])`` (prepared as one
+    weight, or the parts' prepared weights concatenated with their scales),
+    ``bias`` the concatenated biases or None.  One quantizer launch and one
+    GEMM whose drain dequantizes each part straight into its own output --
+    bit-identical to ``linear_acc`` followed by :func:`dequant_slice` per part
+    (the reference's pattern, ops.py:500-525 with selftest.py:67-72), without
+    the int32 [M, parts*N] accumulator round trip through HBM.
+    """
+    reason = unsupported_reason(x, w8, w_scale, act)
+    if reason is not None:
+        raise TypeError(reason)
+    m, n_all, k = _dims(x, w8, act)
+    if parts < 1 or parts > 8 or n_all % parts:
+        raise ValueError(f"{n_all} output channels do not split into {parts} equal parts "
+                         f"(1 <= parts <= 8)")
+    n = n_all // parts
+    if n % 32:
+        raise ValueError(f"each part's width must be a multiple of 32 (got {n})")
+    x2 = x.reshape(m, -1)
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(dtype=torch.bfloat16)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    lib = _lib()
+    dev = x.device
+    ws = expand_scale(w_scale, n_all, dev)
+    b = None if bias is None else expand_scale(bias, n_all, dev)
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
+    outs = [torch.empty((m, n), dtype=torch.bfloat16, device=dev) for _ in range(parts)]
+    table = (ctypes.c_void_p * parts)(*[o.data_ptr() for o in outs])
+    w8c = w8 if w8.is_contiguous() else w8.contiguous()
+    rc = lib.xpuint8_linear_split_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws), _ptr(b),
+                                         table, parts, _ptr(xq), _ptr(xs), m, n, k,
+                                         0 if act is None else ACTIVATIONS[act])
+    if rc != 0:
+        _err(lib, "linear_split")
+    return tuple(o.reshape(*x.shape[:-1], n) for o in outs)
 
 
 def ffn(x, up_w8, up_scale, down_w8, down_scale, down_bias=None, act="situ"):

@@ -1,163 +1,254 @@
 """``python -m xpu_kernels``: does the library work on this machine?
 
-The B200 build of the reference's self-test (python/xpu_kernels/int8/selftest.py)
-with the same checks and pass thresholds (:157-163), plus the int32 GEMM
-against an exact reference and the int8 weight gradient:
-
-* INT8 linear vs the bf16 matmul: relative error < 0.02
-* ``dequant(linear_acc(x))`` == ``linear(x)`` bit for bit; strided slice == contiguous
-* fused situ epilogue vs the unfused chain: codes within 1
-* fused GEGLU FFN == the unfused chain ``quantize(hidden * gelu(gate))`` bit for bit
-* backward: dx conventions exact, dequant_weight == its torch chain, dx_int8 < 0.04,
-  quantize_row == quantize_row_torch with exact scales, autograd dx/dW < 1e-6
-* trainable linear: forward == the INT8 model, dW == the bf16 model
-* int8 GEMM == an fp64 reference exactly; int8 dW within 0.04 of the bf16 dW
+A table of named checks, each run through this build's C entry points on the
+current CUDA device and judged against a stated gate.  The seeded problem
+(x [512, 1024], W [512, 1024], a 1024-wide FFN) and the pass thresholds are the
+reference self-test's contract (python/xpu_kernels/int8/selftest.py:52-56 for
+the shapes and scales, :157-163 for the thresholds); the checks marked "new"
+cover what this build adds (the exact int8 GEMM, the fused qkv split, the int8
+weight gradient, the bounded-wait fault word).  ``run_checks`` returns one
+record per check; ``selftest`` prints them and returns True when all pass.
 """
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+from typing import Callable, List
+
 import torch
 
-from ._lib import _ERR, available, device_name
-from .ops import (
-    TrainableInt8Linear,
-    dequant,
-    dequant_act_quantize,
-    dequant_slice,
-    dequant_weight,
-    dequant_weight_torch,
-    ffn,
-    int8_linear,
-    int_mm,
-    linear,
-    linear_acc,
-    linear_dw,
-    linear_dw_int8,
-    linear_dx,
-    linear_dx_int8,
-    prepare_weight,
-    prepare_weight_fused,
-    quantize,
-    quantize_act,
-    quantize_row,
-    quantize_row_torch,
-)
+from . import _lib as L
+from . import ops
 
 
-def _rel(a, b):
+@dataclass
+class Check:
+    name: str
+    gate: str                       # the pass condition, in words
+    source: str                     # the reference line whose gate it keeps, or "new"
+    run: Callable[["_Problem"], tuple]   # -> (measured value, passed)
+
+
+def _rel(a, b) -> float:
     return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
 
 
-def selftest(verbose: bool = True) -> bool:
-    """Quick end-to-end check on this machine.  Returns True when it passes."""
-    if not available():
-        if verbose:
-            from . import _lib as L
-            print(f"libxpuint8 unavailable: {L._ERR or _ERR}")
-        return False
+def _bits_equal(a, b) -> bool:
+    return bool(a.view(torch.int16).equal(b.view(torch.int16)))
+
+
+class _Problem:
+    """The seeded inputs of the self-test and the results several checks share,
+    computed once on first use."""
+
+    M, K, N, FF = 512, 1024, 512, 1024
+
+    def __init__(self, dev):
+        self.dev = dev
+        g = torch.Generator(device=dev).manual_seed(0)
+
+        def randn(*shape, scale):
+            return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+        self.x = randn(self.M, self.K, scale=0.5)
+        self.w = randn(self.N, self.K, scale=0.05)
+        self.bias = torch.randn(self.N, generator=g, device=dev) * 0.1
+        self.w_up = randn(2 * self.FF, self.K, scale=0.05)
+        self.x_up = randn(self.M, self.K, scale=0.5)
+        self.w_down = randn(self.K, self.FF, scale=0.05)
+        self.dy = randn(self.M, self.N, scale=0.5)
+        self.w8, self.ws = ops.prepare_weight(self.w)
+        self.up8, self.up_s = ops.prepare_weight(self.w_up)
+        self.down8, self.down_s = ops.prepare_weight(self.w_down)
+        self.y = ops.linear(self.x, self.w8, self.ws, self.bias)
+        self.xq, self.xs = ops.quantize(self.x)
+        self.w_deq = ops.dequant_weight(self.w8, self.ws)
+        xr = self.x.detach().clone().requires_grad_(True)
+        torch.nn.functional.linear(xr, self.w).backward(self.dy)
+        self.dx_autograd = xr.grad
+        # dW of the dequantized weight by autograd
+        xa = self.x.detach().clone().requires_grad_(True)
+        wa = self.w_deq.detach().clone().requires_grad_(True)
+        torch.nn.functional.linear(xa, wa).backward(self.dy)
+        self.dw_autograd = wa.grad
+
+
+# ---------------------------------------------------------------- the checks
+
+def _linear_vs_bf16(p):
+    ref = (p.x.float() @ p.w.float().t() + p.bias).to(torch.bfloat16)
+    r = _rel(p.y, ref)
+    return r, r < 0.02
+
+
+def _acc_path_is_linear(p):
+    acc, xs = ops.linear_acc(p.x, p.w8, p.ws)
+    same = _bits_equal(ops.dequant(acc, xs, p.ws, p.bias), p.y)
+    return same, same
+
+
+def _gemm_exact(p):
+    acc = ops.int_mm(p.xq, p.w8)
+    exact = bool(acc.equal((p.xq.double() @ p.w8.double().t()).to(torch.int32)))
+    return exact, exact
+
+
+def _strided_slice(p):
+    acc2, xs2 = ops.linear_acc(p.x, torch.cat([p.w8, p.w8]), torch.cat([p.ws, p.ws]))
+    left = acc2[:, :p.N]
+    same = _bits_equal(ops.dequant_slice(left, xs2, p.ws, p.bias),
+                       ops.dequant(left.contiguous(), xs2, p.ws, p.bias))
+    return same, same
+
+
+def _split_projection(p):
+    w3 = torch.cat([p.w8, p.w8, p.w8])
+    s3 = torch.cat([p.ws, p.ws, p.ws])
+    b3 = torch.cat([p.bias, p.bias * 2, p.bias * 3])
+    parts = ops.linear_split(p.x, w3, s3, b3, parts=3)
+    same = all(_bits_equal(t, ops.linear(p.x, p.w8, p.ws, p.bias * (i + 1)))
+               for i, t in enumerate(parts))
+    return same, same
+
+
+def _situ_epilogue(p):
+    acc, xs = ops.linear_acc(p.x_up, p.up8, p.up_s)
+    q, s = ops.dequant_act_quantize(acc, xs, p.up_s, "situ")
+    q_ref, s_ref = ops.quantize_act(ops.dequant(acc, xs, p.up_s), "situ")
+    code = int((q.to(torch.int16) - q_ref.to(torch.int16)).abs().max())
+    srel = float(((s - s_ref).abs() / s_ref.clamp_min(1e-20)).max())
+    return (code, round(srel, 5)), code <= 1 and srel < 0.05
+
+
+def _geglu_ffn(p):
+    fused = ops.ffn(p.x_up, p.up8, p.up_s, p.down8, p.down_s, act="geglu_erf")
+    acc, xs = ops.linear_acc(p.x_up, p.up8, p.up_s)
+    hidden, gate = ops.dequant(acc, xs, p.up_s).chunk(2, dim=-1)
+    q2, xs2 = ops.quantize(hidden * torch.nn.functional.gelu(gate))
+    chain = ops.dequant(ops.int_mm(q2, p.down8), xs2, p.down_s)
+    differ = int((fused.view(torch.int16) != chain.view(torch.int16)).sum())
+    return differ, differ == 0
+
+
+def _dx_dense(p):
+    r = _rel(ops.linear_dx(p.dy, p.w), p.dx_autograd)
+    return r, r < 1e-6
+
+
+def _dequant_weight(p):
+    same = _bits_equal(p.w_deq, ops.dequant_weight_torch(p.w8, p.ws))
+    r = _rel(p.w_deq, p.w)
+    return (same, round(r, 5)), same and r < 0.02
+
+
+def _dx_int8_weight(p):
+    r = _rel(ops.linear_dx(p.dy, p.w_deq), p.dx_autograd)
+    return r, r < 0.03
+
+
+def _dx_int8_gemm(p):
+    r = _rel(ops.linear_dx_int8(p.dy, p.w8, p.ws), p.dx_autograd)
+    return r, r < 0.04
+
+
+def _row_quantizer(p):
+    q, s = ops.quantize_row(p.dy)
+    qt, st = ops.quantize_row_torch(p.dy)
+    differ = int((q != qt).sum())
+    scales = bool(s.view(torch.int32).equal(st.view(torch.int32)))
+    return (differ, scales), differ == 0 and scales
+
+
+def _autograd_op(p):
+    xi = p.x.detach().clone().requires_grad_(True)
+    ops.int8_linear(xi, p.w8, p.ws, None, mode="dense").backward(p.dy)
+    r_dx = _rel(xi.grad, p.dy @ p.w_deq)
+    r_dw = _rel(ops.linear_dw(p.dy, p.x), p.dw_autograd)
+    return (r_dx, r_dw), r_dx < 1e-6 and r_dw < 1e-6
+
+
+def _dw_int8(p):
+    r = _rel(ops.linear_dw_int8(p.dy, p.xq, p.xs), p.dw_autograd)
+    return r, r < 0.04
+
+
+def _trainable(p):
+    mod = ops.TrainableInt8Linear(p.w, p.bias)
+    y = mod(p.x)
+    w8f, wsf = ops.prepare_weight_fused(p.w)
+    fwd = _bits_equal(y, ops.linear(p.x, w8f, wsf, mod.bias.detach()))
+    y.backward(p.dy)
+    dw = _bits_equal(mod.weight.grad, ops.linear_dw(p.dy, p.x))
+    return (fwd, dw), fwd and dw
+
+
+def _fault_word(p):
+    torch.cuda.synchronize(p.dev)
+    word = L.load().xpuint8_fault_status(0)
+    return word, word == 0
+
+
+CHECKS: List[Check] = [
+    Check("linear vs bf16 matmul", "relative error < 0.02", "selftest.py:157", _linear_vs_bf16),
+    Check("accumulator path", "dequant(linear_acc(x)) == linear(x), bit for bit",
+          "selftest.py:157", _acc_path_is_linear),
+    Check("int8 GEMM", "int32 result == the fp64 product exactly", "new", _gemm_exact),
+    Check("strided dequant slice", "== the contiguous copy's dequant, bit for bit",
+          "selftest.py:157", _strided_slice),
+    Check("fused qkv split", "each part == linear() of that part, bit for bit", "new",
+          _split_projection),
+    Check("fused situ epilogue", "codes within 1 and scales within 5 % of the unfused chain",
+          "selftest.py:157-158", _situ_epilogue),
+    Check("fused GEGLU FFN", "0 bf16 values differ from quantize(hidden * gelu(gate)) chain",
+          "selftest.py:162", _geglu_ffn),
+    Check("dense dx", "relative error vs autograd < 1e-6", "selftest.py:159", _dx_dense),
+    Check("dequant_weight", "== its torch chain bit for bit; within 0.02 of W",
+          "selftest.py:159-161", _dequant_weight),
+    Check("dx through the int8 weight", "relative error < 0.03", "selftest.py:159",
+          _dx_int8_weight),
+    Check("dx with the int8 GEMM", "relative error < 0.04", "selftest.py:160", _dx_int8_gemm),
+    Check("row quantizer", "codes == quantize_row_torch's; scales bit-identical",
+          "selftest.py:161", _row_quantizer),
+    Check("autograd op", "dx vs the same GEMM and dW vs autograd < 1e-6",
+          "selftest.py:162", _autograd_op),
+    Check("int8 dW", "relative error vs the bf16 dW < 0.04", "new", _dw_int8),
+    Check("trainable linear", "forward == the INT8 model's; dW == the bf16 model's",
+          "selftest.py:162-163", _trainable),
+    Check("device fault word", "no bounded wait gave up", "new", _fault_word),
+]
+
+
+def run_checks() -> List[dict]:
+    """Run every check on the current CUDA device; one record per check:
+    ``{"name", "gate", "source", "measured", "ok"}`` (``ok`` False with the
+    exception text as ``measured`` when a check raises)."""
     dev = torch.device("cuda", torch.cuda.current_device())
-    g = torch.Generator(device=dev).manual_seed(0)
-    M, K, N = 512, 1024, 512
-    x = (torch.randn(M, K, generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    w = (torch.randn(N, K, generator=g, device=dev) * 0.05).to(torch.bfloat16)
-    bias = torch.randn(N, generator=g, device=dev) * 0.1
+    problem = _Problem(dev)
+    out = []
+    for c in CHECKS:
+        try:
+            measured, ok = c.run(problem)
+        except Exception as exc:  # noqa: BLE001 - reported as a failed check
+            measured, ok = f"{type(exc).__name__}: {exc}", False
+        out.append({"name": c.name, "gate": c.gate, "source": c.source,
+                    "measured": measured, "ok": bool(ok)})
+    torch.cuda.synchronize(dev)
+    return out
 
-    w8, ws = prepare_weight(w)
-    y = linear(x, w8, ws, bias)
-    ref = (x.float() @ w.float().t() + bias).to(torch.bfloat16)
-    rel = _rel(y, ref)
 
-    acc, xs = linear_acc(x, w8, ws)
-    same = dequant(acc, xs, ws, bias).view(torch.int16).equal(y.view(torch.int16))
-
-    xq, _ = quantize(x)
-    acc_ref = (xq.double() @ w8.double().t()).to(torch.int32)
-    gemm_exact = bool(acc.equal(acc_ref))
-
-    acc_w, xs_w = linear_acc(x, torch.cat([w8, w8], 0), torch.cat([ws, ws]))
-    half = acc_w[:, :N]
-    sl = dequant_slice(half, xs_w, ws, bias)
-    slice_same = sl.view(torch.int16).equal(dequant(half.contiguous(), xs_w, ws, bias).view(torch.int16))
-
-    kff = 1024
-    wup = (torch.randn(2 * kff, K, generator=g, device=dev) * 0.05).to(torch.bfloat16)
-    wup8, wup_s = prepare_weight(wup)
-    xup = (torch.randn(M, K, generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    acc2, xs2 = linear_acc(xup, wup8, wup_s)
-    q2, s2 = dequant_act_quantize(acc2, xs2, wup_s)
-    d = dequant(acc2, xs2, wup_s)
-    q2_ref, s2_ref = quantize_act(d, "situ")
-    code_diff = int((q2.to(torch.int16) - q2_ref.to(torch.int16)).abs().max())
-    scale_rel = float(((s2 - s2_ref).abs() / s2_ref.clamp_min(1e-20)).max())
-
-    wdown = (torch.randn(K, kff, generator=g, device=dev) * 0.05).to(torch.bfloat16)
-    wdown8, wdown_s = prepare_weight(wdown)
-    ffn_fused = ffn(xup, wup8, wup_s, wdown8, wdown_s, act="geglu_erf")
-    hidden, gate = d.chunk(2, dim=-1)
-    q2_g, xs2_g = quantize(hidden * torch.nn.functional.gelu(gate))
-    ffn_ref = dequant(int_mm(q2_g, wdown8), xs2_g, wdown_s)
-    geglu_diff = int((ffn_fused.view(torch.int16) != ffn_ref.view(torch.int16)).sum())
-
-    dy = (torch.randn(M, N, generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    xr = x.detach().clone().requires_grad_(True)
-    torch.nn.functional.linear(xr, w).backward(dy)
-    grad = xr.grad
-    dx_rel = _rel(linear_dx(dy, w), grad)
-    w_deq = dequant_weight(w8, ws)
-    dequant_same = bool(w_deq.view(torch.int16).eq(dequant_weight_torch(w8, ws).view(torch.int16)).all())
-    w_rel = _rel(w_deq, w)
-    dx_int8_rel = _rel(linear_dx(dy, w_deq), grad)
-    dx_q_rel = _rel(linear_dx_int8(dy, w8, ws), grad)
-
-    q_fused, s_fused = quantize_row(dy)
-    q_chain, s_chain = quantize_row_torch(dy)
-    quant_diff = int((q_fused.view(torch.int8) != q_chain.view(torch.int8)).sum())
-    quant_rel = _rel(q_fused, q_chain)
-    scale_same = bool(s_fused.view(torch.int32).equal(s_chain.view(torch.int32)))
-
-    xi = x.detach().clone().requires_grad_(True)
-    int8_linear(xi, w8, ws, None, mode="dense").backward(dy)
-    dx_gemm_rel = _rel(xi.grad, dy @ w_deq)
-    dw = linear_dw(dy, x)
-    xr2 = x.detach().clone().requires_grad_(True)
-    wr2 = w_deq.detach().clone().requires_grad_(True)
-    torch.nn.functional.linear(xr2, wr2).backward(dy)
-    dw_rel = _rel(dw, wr2.grad)
-    dw_int8_rel = _rel(linear_dw_int8(dy, xq, xs), wr2.grad)
-
-    tr = TrainableInt8Linear(w, bias)
-    y_tr = tr(x)
-    w8_f, ws_f = prepare_weight_fused(w)
-    y_tr_ref = linear(x, w8_f, ws_f, tr.bias.detach())
-    tr_same = bool(y_tr.view(torch.int16).eq(y_tr_ref.view(torch.int16)).all())
-    y_tr.backward(dy)
-    dw_same = bool(tr.weight.grad.view(torch.int16).eq(dw.view(torch.int16)).all())
-    torch.cuda.synchronize()
-
-    ok = (same and slice_same and gemm_exact and rel < 0.02 and code_diff <= 1
-          and scale_rel < 0.05 and dx_rel < 1e-6 and w_rel < 0.02 and dx_int8_rel < 0.03
-          and dx_q_rel < 0.04 and quant_diff == 0 and scale_same and dequant_same
-          and dx_gemm_rel < 1e-6 and dw_rel < 1e-6 and geglu_diff == 0 and tr_same
-          and dw_same and dw_int8_rel < 0.04)
+def selftest(verbose: bool = True) -> bool:
+    """Quick end-to-end check on this machine.  Returns True when every check passes."""
+    if not L.available():
+        if verbose:
+            print(f"libxpuint8 unavailable: {L._ERR}")
+        return False
+    records = run_checks()
+    ok = all(r["ok"] for r in records)
     if verbose:
-        print(f"device            : {device_name()}")
-        print(f"INT8 vs bf16      : relative error {rel:.4f} (expect < 0.02)")
-        print(f"acc path == linear: {same}")
-        print(f"int8 GEMM exact   : {gemm_exact}")
-        print(f"strided slice     : {slice_same}")
-        print(f"fused situ vs chain: max code diff {code_diff}, max scale rel {scale_rel:.4f}")
-        print(f"fused GEGLU FFN vs the unfused chain: {geglu_diff} bf16 values differ (expect 0)")
-        print(f"trainable INT8 linear: forward is the INT8 model's {tr_same}, "
-              f"dW is the bf16 model's {dw_same}")
-        print(f"backward dx vs autograd: rel {dx_rel:.2e} (expect 0)")
-        print(f"dequant_weight    : rel {w_rel:.4f} (the INT8 weight itself)")
-        print(f"backward dx, INT8 : rel {dx_int8_rel:.4f}")
-        print(f"backward dx, int8 GEMM (weight stays quantized): rel {dx_q_rel:.4f}")
-        print(f"backward dW, int8 GEMM: rel {dw_int8_rel:.4f}")
-        print(f"fused quantizer vs chain: {quant_diff} of {q_fused.numel()} values "
-              f"differ, rel {quant_rel:.2e}, scales exact: {scale_same}")
-        print(f"fused dequant vs the chain: bit-identical {dequant_same}")
-        print(f"autograd op: dx vs the same GEMM rel {dx_gemm_rel:.2e}, "
-              f"dW vs autograd rel {dw_rel:.2e}")
+        print(f"device: {L.device_name()}")
+        width = max(len(r["name"]) for r in records)
+        for r in records:
+            print(f"  {'ok  ' if r['ok'] else 'FAIL'} {r['name']:<{width}}  {r['measured']!s:<28} "
+                  f"[{r['gate']}; {r['source']}]")
         print("PASS" if ok else "FAIL")
     return ok

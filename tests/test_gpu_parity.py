@@ -589,6 +589,9 @@ def test_geglu_ffn_equals_the_unfused_chain():
 
 def test_selftest_passes():
     from xpu_kernels import int8
+    from xpu_kernels.int8.selftest import run_checks
+    failed = [r for r in run_checks() if not r["ok"]]
+    assert not failed, failed
     assert int8.selftest(verbose=True)
 
 
@@ -711,3 +714,46 @@ def test_allgather_ragged_blocks_on_one_gpu(m, widths, k):
     torch.cuda.synchronize()
     for o in outs:
         assert torch.equal(o.view(torch.int16), full.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,n,k,with_bias", [(2048, 1280, 1280, True), (333, 96, 512, False),
+                                             (1, 64, 256, True)])
+def test_split_projection_equals_acc_and_slices(m, n, k, with_bias):
+    """The fused qkv projection (one GEMM over cat(Wq, Wk, Wv), each third
+    dequantized straight into its own output) is bit-identical to the
+    reference's pattern: linear_acc, then dequant_slice of each third
+    (python/xpu_kernels/int8/selftest.py:67-72), and to a linear per part."""
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 200 + m, outliers=6).to(DEV)
+    ws_parts, w8_parts = [], []
+    for i in range(3):
+        _, w8i, wsi = _prep(n, k, 201 + i)
+        w8_parts.append(torch.from_numpy(w8i).to(DEV))
+        ws_parts.append(torch.from_numpy(wsi).to(DEV))
+    w8, ws = torch.cat(w8_parts), torch.cat(ws_parts)
+    g = torch.Generator().manual_seed(n)
+    bias = (torch.randn(3 * n, generator=g) * 0.01).to(DEV) if with_bias else None
+    q, kk, v = int8.linear_split(x, w8, ws, bias, parts=3)
+    acc, xs = int8.linear_acc(x, w8, ws)
+    for i, got in enumerate((q, kk, v)):
+        sl = slice(i * n, (i + 1) * n)
+        ref = int8.dequant_slice(acc[:, sl], xs, ws[sl], None if bias is None else bias[sl])
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), i
+        one = int8.linear(x, w8_parts[i], ws_parts[i], None if bias is None else bias[sl])
+        assert torch.equal(got.view(torch.int16), one.view(torch.int16)), i
+    # and the oracle on a few rows
+    rows = np.arange(0, m, max(1, m // 7))
+    ref_all = O.linear(bits(x)[rows], bits(w8), bits(ws), None if bias is None else bits(bias))
+    got_all = np.concatenate([bits(t)[rows] for t in (q, kk, v)], axis=1)
+    assert np.array_equal(got_all, ref_all)
+
+
+def test_split_projection_rejects_bad_parts():
+    from xpu_kernels import int8
+    x = rand_bf16((4, 256), 1).to(DEV)
+    w8 = torch.zeros((3 * 48, 256), dtype=torch.int8, device=DEV)
+    ws = torch.ones(3 * 48, device=DEV)
+    with pytest.raises(ValueError):
+        int8.linear_split(x, w8, ws, parts=3)      # 48 columns: not a multiple of 32
+    with pytest.raises(ValueError):
+        int8.linear_split(x, w8, ws, parts=5)      # 144 rows do not split in 5
