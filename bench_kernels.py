@@ -30,16 +30,29 @@ from xpu_kernels.int8._lib import _lib, _ptr, _stream  # noqa: E402
 
 
 def _time(fn, iters, stream):
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    """Device time per call (ms): the `iters` calls captured in a CUDA graph
+    (after eager warm-up calls), the graph replayed three times between CUDA
+    events.  Host-side launch overhead is not in the number."""
     for i in range(min(3, iters)):
         fn(i)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(iters):
+                fn(i)
+    stream.wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(iters):
-        fn(i)
+    for _ in range(3):
+        graph.replay()
     e1.record(stream)
     e1.synchronize()
-    return e0.elapsed_time(e1) / iters
+    return e0.elapsed_time(e1) / (3 * iters)
 
 
 # The shapes of the BASELINE configs (C3 W1, C3 GEGLU, C4 backward, C5), run by
@@ -82,7 +95,6 @@ def main(argv=None):
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib()
     st = torch.cuda.current_stream(dev)
-    sp = _stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     M, N, K = a.M, a.N, a.K
 
@@ -110,12 +122,12 @@ def main(argv=None):
         def fn(i):
             j = i % S
             if a.case == "gemm_raw":
-                rc = lib.xpuint8_int_mm_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]), M, N, K, 0, N)
+                rc = lib.xpuint8_int_mm_stream(_stream(dev), _ptr(A[j]), _ptr(B[j]), _ptr(O[j]), M, N, K, 0, N)
             elif a.case == "geglu":
-                rc = lib.xpuint8_int_mm_geglu_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
+                rc = lib.xpuint8_int_mm_geglu_stream(_stream(dev), _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
                                                      _ptr(xs), _ptr(ws), M, N, K)
             else:
-                rc = lib.xpuint8_int_mm_dequant_stream(sp, _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
+                rc = lib.xpuint8_int_mm_dequant_stream(_stream(dev), _ptr(A[j]), _ptr(B[j]), _ptr(O[j]),
                                                        _ptr(xs), _ptr(ws), _ptr(bias), M, N, K,
                                                        lay, N)
             assert rc == 0, lib.xpuint8_last_error()
@@ -131,11 +143,11 @@ def main(argv=None):
         def fn(i):
             j = i % S
             if a.case == "rotate_quant":
-                rc = lib.xpuint8_convrot_quantize_stream(sp, _ptr(X[j]), _ptr(Q[j]), _ptr(sc[j]), M, K)
+                rc = lib.xpuint8_convrot_quantize_stream(_stream(dev), _ptr(X[j]), _ptr(Q[j]), _ptr(sc[j]), M, K)
             elif a.case == "rotate":
-                rc = lib.xpuint8_convrot_rotate_bf16_stream(sp, _ptr(X[j]), _ptr(Q[j]), M, K)
+                rc = lib.xpuint8_convrot_rotate_bf16_stream(_stream(dev), _ptr(X[j]), _ptr(Q[j]), M, K)
             else:
-                rc = lib.xpuint8_quantize_row_stream(sp, _ptr(X[j]), None, _ptr(Q[j]), _ptr(sc[j]), M, K)
+                rc = lib.xpuint8_quantize_row_stream(_stream(dev), _ptr(X[j]), None, _ptr(Q[j]), _ptr(sc[j]), M, K)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = (4 * M * K) if a.case == "rotate" else (3 * M * K + 4 * M)
         t = _time(fn, a.iters, st)
@@ -148,7 +160,7 @@ def main(argv=None):
 
         def fn(i):
             j = i % S
-            rc = lib.xpuint8_dequant_epilogue_stream(sp, _ptr(ACC[j]), _ptr(O[j]), _ptr(xs), _ptr(ws),
+            rc = lib.xpuint8_dequant_epilogue_stream(_stream(dev), _ptr(ACC[j]), _ptr(O[j]), _ptr(xs), _ptr(ws),
                                                      _ptr(bias), M, N)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = 6 * M * N + 4 * M + 12 * N
@@ -163,7 +175,7 @@ def main(argv=None):
 
         def fn(i):
             j = i % S
-            rc = lib.xpuint8_dequant_act_quantize_stream(sp, _ptr(ACC[j]), _ptr(Q[j]), _ptr(sc[j]),
+            rc = lib.xpuint8_dequant_act_quantize_stream(_stream(dev), _ptr(ACC[j]), _ptr(Q[j]), _ptr(sc[j]),
                                                          _ptr(xs), _ptr(ws), M, K, 4)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = 8 * M * K + 8 * K + M * K + 8 * M

@@ -125,9 +125,10 @@ struct WorkIter {
 __device__ __forceinline__ int64_t sk_start(int q, int64_t W, int npairs) {
     return static_cast<int64_t>(q) * W / npairs;
 }
+template <bool SK>
 __device__ __forceinline__ WorkIter work_begin(const GemmArgs &a, int pair, int npairs) {
     WorkIter it;
-    if (a.sk) {
+    if constexpr (SK) {
         const int64_t W = static_cast<int64_t>(a.num_m) * a.num_n * a.num_k;
         it.cur = sk_start(pair, W, npairs);
         it.end = sk_start(pair + 1, W, npairs);
@@ -139,10 +140,11 @@ __device__ __forceinline__ WorkIter work_begin(const GemmArgs &a, int pair, int 
     }
     return it;
 }
+template <bool SK>
 __device__ __forceinline__ bool work_next(const GemmArgs &a, WorkIter &it, int &tile, int &kb0,
                                           int &kb1) {
     if (it.cur >= it.end) return false;
-    if (a.sk) {
+    if constexpr (SK) {
         tile = static_cast<int>(it.cur / a.num_k);
         kb0 = static_cast<int>(it.cur - static_cast<int64_t>(tile) * a.num_k);
         const int64_t tile_end = static_cast<int64_t>(tile + 1) * a.num_k;
@@ -361,7 +363,7 @@ __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
 // Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
 // quarter) x columns [c0, c1), 32 columns at a time; with sk.n > 0 the other
 // stream-K pieces' partial sums are added to the accumulators first.
-template <int EPI>
+template <int EPI, bool SK>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &tmOut, uint32_t taddr,
                                               int m0, int n0, int quarter, int c0, int c1, int lane,
                                               float xs, const float *s_ws, const float *s_b,
@@ -382,11 +384,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             const uint32_t buf = bufs + bsel * kStageBytes;
             float v[32];
             tmem_wait_ld(r0);
-            if (sk.n) sk_add32(r0, sk, c);
+            if (SK && sk.n) sk_add32(r0, sk, c);
             dequant32(r0, s_ws + c, s_b + c, xs2, bias, v);
             stage_bf16_32_wide(buf, lane, 0, v);
             tmem_wait_ld(r1);
-            if (sk.n) sk_add32(r1, sk, c + 32);
+            if (SK && sk.n) sk_add32(r1, sk, c + 32);
             dequant32(r1, s_ws + c + 32, s_b + c + 32, xs2, bias, v);
             stage_bf16_32_wide(buf, lane, 1, v);
             stage_flush(tmOut, buf, lane, n0 + c, y, a.split_n);
@@ -400,7 +402,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
         tmem_ld32(taddr + c, r);
         if constexpr (EPI == kEpiRawI32) {
             tmem_wait_ld(r);
-            if (sk.n) sk_add32(r, sk, c);
+            if (SK && sk.n) sk_add32(r, sk, c);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 stage_reserve(lane);
@@ -416,14 +418,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             float v[32];
             if constexpr (EPI == kEpiDequantBf16) {
                 tmem_wait_ld(r);
-                if (sk.n) sk_add32(r, sk, c);
+                if (SK && sk.n) sk_add32(r, sk, c);
                 dequant32(r, s_ws + c, s_b + c, xs2, bias, v);
             } else {
                 uint32_t rg[32];
                 tmem_ld32(taddr + 128 + c, rg);
                 tmem_wait_ld(r);
                 tmem_wait_ld(rg);
-                if (sk.n) {
+                if (SK && sk.n) {
                     sk_add32(r, sk, c);
                     sk_add32(rg, sk, 128 + c);
                 }
@@ -439,7 +441,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
     }
 }
 
-template <int EPI, bool A_MN, bool B_MN>
+template <int EPI, bool A_MN, bool B_MN, bool SK>
 __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ OutMaps tmOut, const GemmArgs args) {
@@ -543,9 +545,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             // expect_tx, which the barrier's transaction count allows)
             uint32_t pre = 0;
             if (args.b_early) {
-                WorkIter pit = work_begin(args, pair, npairs);
+                WorkIter pit = work_begin<SK>(args, pair, npairs);
                 int tile, kb0, kb1;
-                while (pre < static_cast<uint32_t>(STAGES) && work_next(args, pit, tile, kb0, kb1)) {
+                while (pre < static_cast<uint32_t>(STAGES) && work_next<SK>(args, pit, tile, kb0, kb1)) {
                     int mb, nb;
                     tile_coords(tile, args.num_m, args.num_n, mb, nb);
                     for (int kb = kb0; kb < kb1 && pre < static_cast<uint32_t>(STAGES); ++kb, ++pre)
@@ -554,9 +556,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             }
             pdl_wait();
             bool ok = true;
-            WorkIter it = work_begin(args, pair, npairs);
+            WorkIter it = work_begin<SK>(args, pair, npairs);
             int tile, kb0, kb1;
-            while (ok && work_next(args, it, tile, kb0, kb1)) {
+            while (ok && work_next<SK>(args, it, tile, kb0, kb1)) {
                 int mb, nb;
                 tile_coords(tile, args.num_m, args.num_n, mb, nb);
                 const int arow = mb * (2 * BM) + static_cast<int>(rank) * BM;
@@ -590,9 +592,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             int acc = 0;
             uint32_t aph = 0;
             bool ok = true;
-            WorkIter it = work_begin(args, pair, npairs);
+            WorkIter it = work_begin<SK>(args, pair, npairs);
             int tile, kb0, kb1;
-            while (ok && work_next(args, it, tile, kb0, kb1)) {
+            while (ok && work_next<SK>(args, it, tile, kb0, kb1)) {
                 if (!mbar_wait(TEMPTY(acc), aph ^ 1u, fault, 2)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -664,9 +666,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         float pre_w = 1.f, pre_b = 0.f;
         const bool stager = et < 2 * BM;
         const int row_local = quarter * 32 + lane;  // accumulator row within this CTA half
-        WorkIter it = work_begin(args, pair, npairs);
+        WorkIter it = work_begin<SK>(args, pair, npairs);
         int tile, kb0, kb1;
-        bool have = work_next(args, it, tile, kb0, kb1);
+        bool have = work_next<SK>(args, it, tile, kb0, kb1);
         if (!args.b_early) pdl_wait();
         if (stager && have) fetch(tile, pre_w, pre_b);
         if (args.b_early) pdl_wait();
@@ -674,19 +676,19 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         while (have) {
             WorkIter nit = it;
             int ntile = 0, nkb0 = 0, nkb1 = 0;
-            const bool nhave = work_next(args, nit, ntile, nkb0, nkb1);
+            const bool nhave = work_next<SK>(args, nit, ntile, nkb0, nkb1);
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
             const int n0 = nb * BN_OUT;
             const int m0 = mb * (2 * BM) + static_cast<int>(rank) * BM;
-            const bool whole = kb0 == 0 && kb1 == args.num_k;
+            const bool whole = !SK || (kb0 == 0 && kb1 == args.num_k);
             if (!epi_sync(5)) break;  // everyone is done with the previous tile's scales
             if (stager) {
                 s_ws[et] = pre_w;
                 s_b[et] = pre_b;
             }
             int *counter = nullptr;
-            if (!whole) {
+            if constexpr (SK) if (!whole) {
                 // this tile's pieces: the pairs whose ranges meet its k-blocks
                 const int64_t u0 = static_cast<int64_t>(tile) * args.num_k;
                 const int q_lo = sk_owner(u0, sk_w, npairs);
@@ -714,7 +716,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
                                    static_cast<uint32_t>(acc * BN);
             SkAdd sk{args.sk_partials, sk_sh + 2, 0, row_local};
             bool finish = true;
-            if (!whole) {
+            if constexpr (SK) if (!whole) {
                 finish = sk_sh[0] != 0;
                 if (!finish) {
                     // store this piece's partial sums, then count it in; the
@@ -739,9 +741,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
                 }
             }
             if (finish)
-                epilogue_tile<EPI>(args, tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
-                                   s_b, bufs, bsel, sk);
-            if (!whole && finish && et == 0) *counter = 0;  // left zero for the next launch
+                epilogue_tile<EPI, SK>(args, tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
+                                       s_b, bufs, bsel, sk);
+            if (SK && !whole && finish && et == 0) *counter = 0;  // left zero for the next launch
             // hand the accumulator back to the leader's MMA issuer (one arrival per warp)
             tc_fence_before();
             __syncwarp();
@@ -819,21 +821,21 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
     return true;
 }
 
-// CTA pairs that can be resident at once for this kernel (the occupancy is
-// cached per device; the shared-memory attribute is set on every call, so a
-// device reset, which clears it, cannot leave a launch without it)
-template <int EPI, bool A_MN, bool B_MN>
+// CTA pairs that can be resident at once for this kernel (cached per device;
+// launch_inst sets the shared-memory attribute on every launch, so a device
+// reset, which clears it, cannot leave a launch without it)
+template <int EPI, bool A_MN, bool B_MN, bool SK>
 int resident_pairs(int dev) {
-    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
-        return -1;
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN, SK>;
     // atomic: first calls from several host threads may race to fill it (same value)
     static std::atomic<int> cached[32] = {};
     if (dev >= 0 && dev < 32) {
         const int c = cached[dev].load(std::memory_order_relaxed);
         if (c > 0) return c;
     }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
+        return -1;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -851,10 +853,13 @@ int resident_pairs(int dev) {
     return n;
 }
 
-template <int EPI, bool A_MN, bool B_MN>
+template <int EPI, bool A_MN, bool B_MN, bool SK>
 int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const OutMaps &mo,
                 const GemmArgs &a, int pairs) {
-    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN, SK>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
+        return launch_status("gemm (shared memory attribute)");
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -875,32 +880,41 @@ int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, co
     return launch_status("gemm");
 }
 
-template <int EPI, bool A_MN, bool B_MN>
-int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
-                 const OutMaps &mo, const GemmArgs &a, int64_t max_pairs) {
+template <int EPI, bool A_MN, bool B_MN, bool SK>
+int launch_sized1(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
+                  const OutMaps &mo, const GemmArgs &a, int64_t max_pairs) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const int resident = resident_pairs<EPI, A_MN, B_MN>(dev);
+    const int resident = resident_pairs<EPI, A_MN, B_MN, SK>(dev);
     if (resident <= 0) {
         set_error("no CTA pair of the GEMM fits on the device");
         return 5;
     }
     const int pairs = static_cast<int>(max_pairs < resident ? max_pairs : resident);
-    return launch_inst<EPI, A_MN, B_MN>(s, ma, mb, mo, a, pairs);
+    return launch_inst<EPI, A_MN, B_MN, SK>(s, ma, mb, mo, a, pairs);
+}
+// the data-parallel instance, or (a.sk, dequant / GEGLU epilogues only) the stream-K one
+template <int EPI, bool A_MN, bool B_MN>
+int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
+                 const OutMaps &mo, const GemmArgs &a, int64_t max_pairs) {
+    if constexpr (EPI == kEpiDequantBf16 || EPI == kEpiGegluBf16) {
+        if (a.sk) return launch_sized1<EPI, A_MN, B_MN, true>(s, ma, mb, mo, a, max_pairs);
+    }
+    return launch_sized1<EPI, A_MN, B_MN, false>(s, ma, mb, mo, a, max_pairs);
 }
 
-// resident CTA pairs of the kernel instance a call would launch
+// resident CTA pairs of the stream-K kernel instance a call would launch
 int resident_for(int epi, bool a_mn, bool b_mn) {
     int dev = 0;
     cudaGetDevice(&dev);
     switch (epi) {
         case kEpiDequantBf16:
-            if (!a_mn && !b_mn) return resident_pairs<kEpiDequantBf16, false, false>(dev);
-            if (!a_mn && b_mn) return resident_pairs<kEpiDequantBf16, false, true>(dev);
-            if (a_mn && b_mn) return resident_pairs<kEpiDequantBf16, true, true>(dev);
+            if (!a_mn && !b_mn) return resident_pairs<kEpiDequantBf16, false, false, true>(dev);
+            if (!a_mn && b_mn) return resident_pairs<kEpiDequantBf16, false, true, true>(dev);
+            if (a_mn && b_mn) return resident_pairs<kEpiDequantBf16, true, true, true>(dev);
             break;
         case kEpiGegluBf16:
-            return resident_pairs<kEpiGegluBf16, false, false>(dev);
+            return resident_pairs<kEpiGegluBf16, false, false, true>(dev);
         default:
             break;
     }
@@ -931,10 +945,13 @@ Plan plan_gemm(const GemmCall &c) {
     // waves (a persistent pair takes every P-th tile), so the critical path is
     // ceil(tiles / P) tiles; a narrower tile can finish sooner when it fills
     // the last wave better (N = 10240 at M = 2048: 320 tiles of 256 columns
-    // take 5 waves of 74 pairs, 368 tiles of 224 columns also 5 waves of 7/8
-    // the work).  Each tile also costs a fixed drain and hand-over, counted as
-    // 32 columns.  Only a K-major B is narrowed: an MN-major B tile is loaded
-    // as two 128-column boxes.
+    // take 5 waves of 74 pairs, 368 tiles of 224 columns also 5 waves of
+    // slightly shorter tiles).  Only a K-major B is narrowed: an MN-major B
+    // tile is loaded as two 128-column boxes.
+    // Cost per tile k-block in "column" units: a tile's MMAs take nearly the
+    // same time at any width (measured on B200: a 128-wide tile ~0.91x the
+    // time of a 256-wide one), i.e. about kMmaFixed + bn.
+    constexpr int64_t kMmaFixed = 1170;
     int64_t cost_dp = -1;
     // XPUINT8_GEMM_BN=<128..256, multiple of 32> fixes the width (tests, tuning)
     const char *force = std::getenv("XPUINT8_GEMM_BN");
@@ -945,7 +962,7 @@ Plan plan_gemm(const GemmCall &c) {
     } else if (!geglu && !c.b_mn) {
         for (int cand = BN; cand >= 128; cand -= step) {
             const int64_t tiles = num_m * ((c.N + cand - 1) / cand);
-            const int64_t cost = ((tiles + sms - 1) / sms) * kb * (cand + 32);
+            const int64_t cost = ((tiles + sms - 1) / sms) * kb * (kMmaFixed + cand);
             if (cost_dp < 0 || cost < cost_dp) {
                 cost_dp = cost;
                 p.bn = cand;
@@ -954,7 +971,7 @@ Plan plan_gemm(const GemmCall &c) {
     } else {
         const int64_t width = geglu ? 128 : BN;
         const int64_t tiles = num_m * ((c.N + width - 1) / width);
-        cost_dp = ((tiles + sms - 1) / sms) * kb * (BN + 32);
+        cost_dp = ((tiles + sms - 1) / sms) * kb * (kMmaFixed + BN);
     }
     // Stream-K: the k-blocks of 256-wide tiles dealt evenly over the pairs.  A
     // pair's range ends inside at most two tiles, whose partial sums cost about
@@ -978,7 +995,7 @@ Plan plan_gemm(const GemmCall &c) {
         const int64_t pairs =
             std::min<int64_t>(std::min<int64_t>(resident > 0 ? resident : sms, tiles * 4), tiles * kb);
         const int64_t per_pair = (tiles * kb + pairs - 1) / pairs;
-        const int64_t cost_sk = (per_pair + 4) * (BN + 32);
+        const int64_t cost_sk = (per_pair + 4) * (kMmaFixed + BN);
         if (resident > 0 && (force_sk || 10 * cost_sk < 9 * cost_dp)) {
             p.sk = true;
             p.bn = BN;
