@@ -138,19 +138,6 @@ int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
                           const float *w_scale, const float *bias, void *out, int8_t *xq,
                           float *xs, int64_t M, int64_t N, int64_t K, int32_t activation);
 
-/* xpuint8_linear_stream with one caller workspace instead of the two scratch
- * buffers: xq, xs and, when it pays, a stream-K area for the GEMM (shapes with
- * few output tiles, e.g. N = 1280, deal their k-blocks evenly over all SMs and
- * sum the split tiles' int32 partials; results are bit-identical).  The
- * workspace holds xpuint8_linear_workspace_bytes(M, N, K) bytes, 16-byte
- * aligned; its content need not be initialised (the call clears what must
- * start at zero on the stream).  Replaces python/xpu_kernels/int8/ops.py:591-646
- * (linear) in one C call, like xpuint8_linear_stream. */
-int64_t xpuint8_linear_workspace_bytes(int64_t M, int64_t N, int64_t K);
-int xpuint8_linear_ws_stream(const void *stream, const void *x, const int8_t *w8,
-                             const float *w_scale, const float *bias, void *out, void *workspace,
-                             int64_t M, int64_t N, int64_t K, int32_t activation);
-
 /* The INT8 linear against a weight of `nparts` concatenated projections
  * (q, k, v: w8 [nparts*N, K] = cat(Wq, Wk, Wv), w_scale [nparts*N], bias
  * [nparts*N] or NULL) in one GEMM whose drain writes part i's columns straight

@@ -13,7 +13,6 @@
 // as the reference's blocking entries do.
 #include <cuda_runtime.h>
 
-#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -189,47 +188,9 @@ int dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const float 
 // b_early: the kernel launched just before on `s` is this library's activation
 // quantizer (or does not write b, col_scale, bias), so the GEMM may load those
 // before it completes
-// the GemmCall of a GEMM with the given epilogue and operand layout (shape only)
-GemmCall gemm_shape(int epi, int64_t M, int64_t N, int64_t K, int32_t layout) {
-    GemmCall c;
-    c.epilogue = epi;
-    c.M = M; c.N = N; c.K = K;
-    c.a_mn = layout == 2;
-    c.b_mn = layout >= 1;
-    return c;
-}
-// stream-K workspace bytes of such a GEMM (0: it runs data parallel)
-int64_t sk_bytes(int epi, int64_t M, int64_t N, int64_t K, int32_t layout) {
-    return gemm_workspace_bytes(gemm_shape(epi, M, N, K, layout));
-}
-int64_t sk_counter_bytes(int epi, int64_t M, int64_t N, int64_t K, int32_t layout) {
-    return gemm_counter_bytes(gemm_shape(epi, M, N, K, layout));
-}
-// a stream-K area inside an entry's workspace
-struct SkArea {
-    void *ptr = nullptr;
-    int64_t bytes = 0;
-};
-SkArea sk_area(char *ws, size_t off, int64_t bytes) {
-    SkArea a;
-    if (bytes > 0) {
-        a.ptr = ws + off;
-        a.bytes = bytes;
-    }
-    return a;
-}
-// clear the counters of a stream-K area on the stream (before the entry's first kernel)
-int clear_sk_counters(cudaStream_t s, const SkArea &a, int64_t counter_bytes) {
-    if (!a.ptr || counter_bytes <= 0) return 0;
-    if (cudaMemsetAsync(a.ptr, 0, static_cast<size_t>(counter_bytes), s) != cudaSuccess)
-        return launch_status("clearing the stream-K counters");
-    return 0;
-}
-
 int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, void *out,
                   const float *row_scale, const float *col_scale, const float *bias, int64_t M,
-                  int64_t N, int64_t K, int32_t layout, int64_t ldo, bool b_early = false,
-                  const SkArea &sk = SkArea{}) {
+                  int64_t N, int64_t K, int32_t layout, int64_t ldo, bool b_early = false) {
     if (M <= 0 || N <= 0 || K <= 0) {
         set_error("M, N and K must be positive");
         return 2;
@@ -252,9 +213,6 @@ int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, voi
     c.row_scale = row_scale; c.col_scale = col_scale; c.bias = bias;
     c.M = M; c.N = N; c.K = K;
     c.b_early = b_early;
-    c.sk_workspace = sk.ptr;
-    c.sk_workspace_bytes = sk.bytes;
-    c.sk_zeroed = true;  // the entries clear the counters before their first kernel
     c.a_mn = layout == 2;
     c.b_mn = layout >= 1;
     c.lda = c.a_mn ? M : K;
@@ -270,8 +228,7 @@ int int_mm_common(cudaStream_t s, int epi, const int8_t *a, const int8_t *b, voi
 size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 struct FfnLayout {
-    size_t xq, xs, mid, q2, xs2, sk, total;
-    int64_t sk_bytes, sk_counters;
+    size_t xq, xs, mid, q2, xs2, total;
 };
 FfnLayout ffn_layout(int64_t M, int64_t K, int64_t inner, int act) {
     FfnLayout L{};
@@ -283,14 +240,6 @@ FfnLayout ffn_layout(int64_t M, int64_t K, int64_t inner, int act) {
     else off += align256(static_cast<size_t>(M) * inner * (act == 5 ? 4 : 8));  // int32 acc
     L.q2 = off; off += align256(static_cast<size_t>(M) * inner);
     L.xs2 = off; off += align256(static_cast<size_t>(M) * 4);
-    // one stream-K area for the two GEMMs, which run one after the other (the
-    // raw int32 up-projection of situ / GELU-erf runs data parallel)
-    const int64_t up = act == 4 ? sk_bytes(kEpiGegluBf16, M, inner, K, 0) : 0;
-    const int64_t down = sk_bytes(kEpiDequantBf16, M, K, inner, 0);
-    L.sk_bytes = up > down ? up : down;
-    L.sk_counters = std::max(act == 4 ? sk_counter_bytes(kEpiGegluBf16, M, inner, K, 0) : 0,
-                             sk_counter_bytes(kEpiDequantBf16, M, K, inner, 0));
-    L.sk = off; off += align256(static_cast<size_t>(L.sk_bytes));
     L.total = off;
     return L;
 }
@@ -473,41 +422,6 @@ int xpuint8_linear_stream(const void *stream, const void *x, const int8_t *w8,
                          K, 0, N, true);
 }
 
-int64_t xpuint8_linear_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-    if (M <= 0 || N <= 0 || K <= 0) return -1;
-    return static_cast<int64_t>(align256(static_cast<size_t>(M) * K) +
-                                align256(static_cast<size_t>(M) * 4) +
-                                align256(static_cast<size_t>(sk_bytes(kEpiDequantBf16, M, N, K, 0))));
-}
-
-int xpuint8_linear_ws_stream(const void *stream, const void *x, const int8_t *w8,
-                             const float *w_scale, const float *bias, void *out, void *workspace,
-                             int64_t M, int64_t N, int64_t K, int32_t activation) {
-    if (N <= 0 || N % 16 != 0) {
-        set_error("N must be a positive multiple of 16");
-        return 2;
-    }
-    if (M <= 0 || K <= 0) {
-        set_error("M and K must be positive");
-        return 2;
-    }
-    if (!workspace || !aligned16(workspace)) {
-        set_error("the workspace must be a 16-byte aligned buffer");
-        return 2;
-    }
-    cudaStream_t s = as_stream(stream);
-    char *ws = static_cast<char *>(workspace);
-    int8_t *xq = reinterpret_cast<int8_t *>(ws);
-    const size_t xs_off = align256(static_cast<size_t>(M) * K);
-    float *xs = reinterpret_cast<float *>(ws + xs_off);
-    const size_t sk_off = xs_off + align256(static_cast<size_t>(M) * 4);
-    const SkArea sk = sk_area(ws, sk_off, sk_bytes(kEpiDequantBf16, M, N, K, 0));
-    if (int rc = clear_sk_counters(s, sk, sk_counter_bytes(kEpiDequantBf16, M, N, K, 0))) return rc;
-    if (int rc = convrot_quantize(s, x, xq, xs, M, K, activation)) return rc;
-    return int_mm_common(s, kEpiDequantBf16, xq, w8, out, xs, w_scale, bias, M, N, K, 0, N, true,
-                         sk);
-}
-
 int xpuint8_linear_split_stream(const void *stream, const void *x, const int8_t *w8,
                                 const float *w_scale, const float *bias, void *const *outs,
                                 int32_t nparts, int8_t *xq, float *xs, int64_t M, int64_t N,
@@ -570,17 +484,11 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
     float *xs = reinterpret_cast<float *>(ws + L.xs);
     int8_t *q2 = reinterpret_cast<int8_t *>(ws + L.q2);
     float *xs2 = reinterpret_cast<float *>(ws + L.xs2);
-    SkArea sk;
-    if (L.sk_bytes > 0) {
-        sk.ptr = ws + L.sk;
-        sk.bytes = L.sk_bytes;
-    }
-    if (int rc = clear_sk_counters(s, sk, L.sk_counters)) return rc;
     if (int rc = convrot_quantize(s, x, xq, xs, M, K, 0)) return rc;
     if (activation == 4) {
         void *y = ws + L.mid;
         if (int rc = int_mm_common(s, kEpiGegluBf16, xq, up_w8, y, xs, up_scale, nullptr, M, inner,
-                                   K, 0, inner, true, sk))
+                                   K, 0, inner, true))
             return rc;
         if (int rc = convrot_quantize(s, y, q2, xs2, M, inner, 0)) return rc;
     } else {
@@ -593,14 +501,13 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
             return rc;
     }
     return int_mm_common(s, kEpiDequantBf16, q2, down_w8, out, xs2, down_scale, down_bias, M, K,
-                         inner, 0, K, true, sk);
+                         inner, 0, K, true);
 }
 
 // ------------------------------------------------------------ fused backward
 namespace {
 struct DxLayout {
-    size_t q, a, dxr, sk, total;
-    int64_t sk_bytes, sk_counters;
+    size_t q, a, dxr, total;
 };
 DxLayout dx_layout(int64_t M, int64_t N, int64_t K) {
     DxLayout L{};
@@ -608,15 +515,11 @@ DxLayout dx_layout(int64_t M, int64_t N, int64_t K) {
     L.q = off; off += align256(static_cast<size_t>(M) * N);       // int8 row-quantized dy
     L.a = off; off += align256(static_cast<size_t>(M) * 4);       // its row scales
     L.dxr = off; off += align256(static_cast<size_t>(M) * K * 2);  // dx before the rotation
-    L.sk_bytes = sk_bytes(kEpiDequantBf16, M, K, N, 1);            // the GEMM's stream-K area
-    L.sk_counters = sk_counter_bytes(kEpiDequantBf16, M, K, N, 1);
-    L.sk = off; off += align256(static_cast<size_t>(L.sk_bytes));
     L.total = off;
     return L;
 }
 struct DwLayout {
-    size_t gq, tg, dwr, sk, total;
-    int64_t sk_bytes, sk_counters;
+    size_t gq, tg, dwr, total;
 };
 DwLayout dw_layout(int64_t M, int64_t N, int64_t K) {
     DwLayout L{};
@@ -624,9 +527,6 @@ DwLayout dw_layout(int64_t M, int64_t N, int64_t K) {
     L.gq = off; off += align256(static_cast<size_t>(M) * N);       // column-quantized dy * xs
     L.tg = off; off += align256(static_cast<size_t>(N) * 4);       // its column scales
     L.dwr = off; off += align256(static_cast<size_t>(N) * K * 2);  // dW before the rotation
-    L.sk_bytes = sk_bytes(kEpiDequantBf16, N, K, M, 2);
-    L.sk_counters = sk_counter_bytes(kEpiDequantBf16, N, K, M, 2);
-    L.sk = off; off += align256(static_cast<size_t>(L.sk_bytes));
     L.total = off;
     return L;
 }
@@ -660,13 +560,11 @@ int xpuint8_linear_dx_int8_stream(const void *stream, const void *dy, const int8
     int8_t *q = reinterpret_cast<int8_t *>(ws + L.q);
     float *a = reinterpret_cast<float *>(ws + L.a);
     void *dxr = ws + L.dxr;
-    const SkArea sk = sk_area(ws, L.sk, L.sk_bytes);
-    if (int rc = clear_sk_counters(s, sk, L.sk_counters)) return rc;
     // d = bf16(dy * bf16(w_scale)) row-quantized in one pass
     if (int rc = launch_quantize_row(s, dy, w_scale, q, a, M, N)) return rc;
     // dxr = bf16(float(q @ w8) * a[m]): w8 [N, K] read as stored (MN-major B)
     if (int rc = int_mm_common(s, kEpiDequantBf16, q, w8, dxr, a, nullptr, nullptr, M, K, N, 1, K,
-                               true, sk))
+                               true))
         return rc;
     // the rotation undone along K
     return launch_rotate_rows(s, 2, 0, dxr, nullptr, nullptr, dx, nullptr, M, K);
@@ -697,13 +595,11 @@ int xpuint8_linear_dw_int8_stream(const void *stream, const void *dy, const int8
     int8_t *gq = reinterpret_cast<int8_t *>(ws + L.gq);
     float *tg = reinterpret_cast<float *>(ws + L.tg);
     void *dwr = ws + L.dwr;
-    const SkArea sk = sk_area(ws, L.sk, L.sk_bytes);
-    if (int rc = clear_sk_counters(s, sk, L.sk_counters)) return rc;
     // g = dy * xs[m] quantized per column n (over the tokens m)
     if (int rc = launch_colquant(s, dy, x_scale, gq, tg, M, N)) return rc;
     // dwr [N, K] = bf16(float(gq^T @ xq) * tg[n]): both operands MN-major
     if (int rc = int_mm_common(s, kEpiDequantBf16, gq, xq, dwr, tg, nullptr, nullptr, N, K, M, 2, K,
-                               true, sk))
+                               true))
         return rc;
     return launch_rotate_rows(s, 2, 0, dwr, nullptr, nullptr, dw, nullptr, N, K);
 }

@@ -46,10 +46,8 @@
 // MMAs (again with a bound), frees its TMEM and returns.
 #include <cuda.h>
 
-#include <algorithm>
 #include <atomic>
 #include <cstdlib>
-#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -82,13 +80,6 @@ struct GemmArgs {
                   // wait for the previous kernel (it does not write them)
     int split_n;  // > 0: output column n goes to destination n / split_n, column
                   // n % split_n (the split projection: q, k, v from one GEMM)
-    // Stream-K schedule (sk != 0): the tiles x num_k k-blocks are dealt to the
-    // pairs as equal contiguous ranges; a tile cut between pairs is summed
-    // from int32 partials in sk_partials by whichever of its pieces finishes
-    // last (counted in sk_counters, which are zero at launch and left zero).
-    int sk;
-    int *sk_counters;       // [tiles][2]: arrivals per tile and CTA half
-    int32_t *sk_partials;   // [2 * pairs][2][128][BN]: each pair's first / last piece
 };
 
 // The output's tensor maps: one per destination.  Either every output tile is
@@ -112,56 +103,6 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     const int local = tile - group * per_group;
     mb = first_m + local % gsz;
     nb = local / gsz;
-}
-
-// The pair's work: a sequence of segments (tile, k-blocks [kb0, kb1)).  Data
-// parallel: every npairs-th tile whole.  Stream-K: units u = tile * num_k + kb
-// in [pair * W / npairs, (pair + 1) * W / npairs), W = tiles * num_k, cut at
-// tile boundaries.  Producer, MMA issuer and epilogue walk the same sequence.
-struct WorkIter {
-    int64_t cur, end;
-    int step;
-};
-__device__ __forceinline__ int64_t sk_start(int q, int64_t W, int npairs) {
-    return static_cast<int64_t>(q) * W / npairs;
-}
-template <bool SK>
-__device__ __forceinline__ WorkIter work_begin(const GemmArgs &a, int pair, int npairs) {
-    WorkIter it;
-    if constexpr (SK) {
-        const int64_t W = static_cast<int64_t>(a.num_m) * a.num_n * a.num_k;
-        it.cur = sk_start(pair, W, npairs);
-        it.end = sk_start(pair + 1, W, npairs);
-        it.step = 0;
-    } else {
-        it.cur = pair;
-        it.end = static_cast<int64_t>(a.num_m) * a.num_n;
-        it.step = npairs;
-    }
-    return it;
-}
-template <bool SK>
-__device__ __forceinline__ bool work_next(const GemmArgs &a, WorkIter &it, int &tile, int &kb0,
-                                          int &kb1) {
-    if (it.cur >= it.end) return false;
-    if constexpr (SK) {
-        tile = static_cast<int>(it.cur / a.num_k);
-        kb0 = static_cast<int>(it.cur - static_cast<int64_t>(tile) * a.num_k);
-        const int64_t tile_end = static_cast<int64_t>(tile + 1) * a.num_k;
-        const int64_t e = it.end < tile_end ? it.end : tile_end;
-        kb1 = kb0 + static_cast<int>(e - it.cur);
-        it.cur = e;
-    } else {
-        tile = static_cast<int>(it.cur);
-        kb0 = 0;
-        kb1 = a.num_k;
-        it.cur += it.step;
-    }
-    return true;
-}
-// the pair whose stream-K range holds unit u
-__device__ __forceinline__ int sk_owner(int64_t u, int64_t W, int npairs) {
-    return static_cast<int>(((u + 1) * npairs - 1) / W);
 }
 
 // bounded wait that ignores other threads' faults: used only to drain our own
@@ -310,64 +251,13 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
     }
 }
 
-// Stream-K partial sums.  A piece of a tile that does not finish it stores its
-// int32 accumulators, row by row, into its slot of args.sk_partials (one
-// [128][BN] block per CTA half); the piece that finishes the tile adds the
-// other pieces' blocks to its own accumulators before the epilogue.
-struct SkAdd {
-    const int32_t *partials;  // args.sk_partials
-    const int *slots;         // shared memory: the other pieces' slots
-    int n;                    // how many (0: nothing to add)
-    int row;                  // this thread's accumulator row within the CTA half
-};
-__device__ __forceinline__ void sk_add32(uint32_t (&r)[32], const SkAdd &sk, int col) {
-    for (int i = 0; i < sk.n; ++i) {
-        const int4 *src = reinterpret_cast<const int4 *>(
-            sk.partials + (static_cast<size_t>(sk.slots[i]) * 128 + sk.row) * BN + col);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int4 v = __ldcg(src + q);  // written by other SMs: read at L2
-            r[4 * q] += static_cast<uint32_t>(v.x);
-            r[4 * q + 1] += static_cast<uint32_t>(v.y);
-            r[4 * q + 2] += static_cast<uint32_t>(v.z);
-            r[4 * q + 3] += static_cast<uint32_t>(v.w);
-        }
-    }
-}
-// this thread's row of accumulator columns [c0, c1) (GEGLU: and the gate
-// columns 128 on) into its partial slot row
-template <int EPI>
-__device__ __forceinline__ void sk_store_partial(uint32_t taddr, int32_t *dst, int c0, int c1) {
-    constexpr int kHalves = EPI == kEpiGegluBf16 ? 2 : 1;
-#pragma unroll
-    for (int h = 0; h < kHalves; ++h) {
-#pragma unroll 1
-        for (int c = c0 + 128 * h; c < c1 + 128 * h; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(taddr + c, r);
-            tmem_wait_ld(r);
-            int4 *d = reinterpret_cast<int4 *>(dst + c);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                __stcg(d + q, make_int4(static_cast<int>(r[4 * q]), static_cast<int>(r[4 * q + 1]),
-                                        static_cast<int>(r[4 * q + 2]), static_cast<int>(r[4 * q + 3])));
-        }
-    }
-}
-__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
-// quarter) x columns [c0, c1), 32 columns at a time; with sk.n > 0 the other
-// stream-K pieces' partial sums are added to the accumulators first.
-template <int EPI, bool SK>
+// quarter) x columns [c0, c1), 32 columns at a time.
+template <int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &tmOut, uint32_t taddr,
                                               int m0, int n0, int quarter, int c0, int c1, int lane,
                                               float xs, const float *s_ws, const float *s_b,
-                                              uint32_t bufs, int &bsel, const SkAdd &sk) {
+                                              uint32_t bufs, int &bsel) {
     const int y = m0 + quarter * 32;
     const f2 xs2 = mk2(xs, xs);
     const bool bias = a.bias != nullptr;
@@ -384,11 +274,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             const uint32_t buf = bufs + bsel * kStageBytes;
             float v[32];
             tmem_wait_ld(r0);
-            if (SK && sk.n) sk_add32(r0, sk, c);
             dequant32(r0, s_ws + c, s_b + c, xs2, bias, v);
             stage_bf16_32_wide(buf, lane, 0, v);
             tmem_wait_ld(r1);
-            if (SK && sk.n) sk_add32(r1, sk, c + 32);
             dequant32(r1, s_ws + c + 32, s_b + c + 32, xs2, bias, v);
             stage_bf16_32_wide(buf, lane, 1, v);
             stage_flush(tmOut, buf, lane, n0 + c, y, a.split_n);
@@ -402,7 +290,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
         tmem_ld32(taddr + c, r);
         if constexpr (EPI == kEpiRawI32) {
             tmem_wait_ld(r);
-            if (SK && sk.n) sk_add32(r, sk, c);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 stage_reserve(lane);
@@ -418,17 +305,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             float v[32];
             if constexpr (EPI == kEpiDequantBf16) {
                 tmem_wait_ld(r);
-                if (SK && sk.n) sk_add32(r, sk, c);
                 dequant32(r, s_ws + c, s_b + c, xs2, bias, v);
             } else {
                 uint32_t rg[32];
                 tmem_ld32(taddr + 128 + c, rg);
                 tmem_wait_ld(r);
                 tmem_wait_ld(rg);
-                if (SK && sk.n) {
-                    sk_add32(r, sk, c);
-                    sk_add32(rg, sk, 128 + c);
-                }
                 geglu32(r, rg, s_ws + c, s_ws + 128 + c, xs2, v);
             }
             stage_reserve(lane);
@@ -441,7 +323,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
     }
 }
 
-template <int EPI, bool A_MN, bool B_MN, bool SK>
+template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ OutMaps tmOut, const GemmArgs args) {
@@ -464,9 +346,6 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     const uint32_t final_bar = bar0 + 8 * (2 * STAGES + 4);
     const uint32_t epi_bar = bar0 + 8 * (2 * STAGES + 5);  // the epilogue threads
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 6);
-    // stream-K hand-off words of the epilogue: [0] "this piece finishes the
-    // tile", [1] the number of other pieces, [2..] their partial slots
-    int *sk_sh = reinterpret_cast<int *>(tmem_slot + 1);
 #define FULL(s) (bar0 + 8u * (s))
 #define EMPTY(s) (bar0 + 8u * (STAGES + (s)))
 #define TFULL(a) (bar0 + 8u * (2 * STAGES + (a)))
@@ -545,24 +424,21 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             // expect_tx, which the barrier's transaction count allows)
             uint32_t pre = 0;
             if (args.b_early) {
-                WorkIter pit = work_begin<SK>(args, pair, npairs);
-                int tile, kb0, kb1;
-                while (pre < static_cast<uint32_t>(STAGES) && work_next<SK>(args, pit, tile, kb0, kb1)) {
+                int tile = pair, kb = 0;
+                for (; pre < static_cast<uint32_t>(STAGES) && tile < num_tiles; ++pre) {
                     int mb, nb;
                     tile_coords(tile, args.num_m, args.num_n, mb, nb);
-                    for (int kb = kb0; kb < kb1 && pre < static_cast<uint32_t>(STAGES); ++kb, ++pre)
-                        load_b(static_cast<int>(pre), nb, kb);
+                    load_b(static_cast<int>(pre), nb, kb);
+                    if (++kb == args.num_k) { kb = 0; tile += npairs; }
                 }
             }
             pdl_wait();
             bool ok = true;
-            WorkIter it = work_begin<SK>(args, pair, npairs);
-            int tile, kb0, kb1;
-            while (ok && work_next<SK>(args, it, tile, kb0, kb1)) {
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 int mb, nb;
                 tile_coords(tile, args.num_m, args.num_n, mb, nb);
                 const int arow = mb * (2 * BM) + static_cast<int>(rank) * BM;
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = 0; kb < args.num_k; ++kb) {
                     if (!mbar_wait(EMPTY(stage), ph ^ 1u, fault, 1)) { ok = false; break; }
                     if (leader) mbar_expect_tx(FULL(stage), pair_tx);
                     const uint32_t fb = peer_smem(FULL(stage), 0);
@@ -592,13 +468,11 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             int acc = 0;
             uint32_t aph = 0;
             bool ok = true;
-            WorkIter it = work_begin<SK>(args, pair, npairs);
-            int tile, kb0, kb1;
-            while (ok && work_next<SK>(args, it, tile, kb0, kb1)) {
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 if (!mbar_wait(TEMPTY(acc), aph ^ 1u, fault, 2)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = 0; kb < args.num_k; ++kb) {
                     if (!mbar_wait(FULL(stage), ph, fault, 3)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a0 = sA + stage * A_BYTES, b0 = sB + stage * B_BYTES;
@@ -610,7 +484,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
                                                  : umma_sdesc_sw128(a0 + kk * 32, 16, 1024);
                         const uint64_t bd = B_MN ? umma_sdesc_sw128(b0 + kk * 4096, BK * 128, 1024)
                                                  : umma_sdesc_sw128(b0 + kk * 32, 16, 1024);
-                        umma_i8_pair(d, ad, bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                        umma_i8_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     // the slot is free in both CTAs once these MMAs have read it
                     umma_commit_pair(EMPTY(stage));
@@ -665,85 +539,29 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         };
         float pre_w = 1.f, pre_b = 0.f;
         const bool stager = et < 2 * BM;
-        const int row_local = quarter * 32 + lane;  // accumulator row within this CTA half
-        WorkIter it = work_begin<SK>(args, pair, npairs);
-        int tile, kb0, kb1;
-        bool have = work_next<SK>(args, it, tile, kb0, kb1);
         if (!args.b_early) pdl_wait();
-        if (stager && have) fetch(tile, pre_w, pre_b);
+        if (stager && pair < num_tiles) fetch(pair, pre_w, pre_b);
         if (args.b_early) pdl_wait();
-        const int64_t sk_w = static_cast<int64_t>(num_tiles) * args.num_k;
-        while (have) {
-            WorkIter nit = it;
-            int ntile = 0, nkb0 = 0, nkb1 = 0;
-            const bool nhave = work_next<SK>(args, nit, ntile, nkb0, nkb1);
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
             int mb, nb;
             tile_coords(tile, args.num_m, args.num_n, mb, nb);
             const int n0 = nb * BN_OUT;
             const int m0 = mb * (2 * BM) + static_cast<int>(rank) * BM;
-            const bool whole = !SK || (kb0 == 0 && kb1 == args.num_k);
             if (!epi_sync(5)) break;  // everyone is done with the previous tile's scales
             if (stager) {
                 s_ws[et] = pre_w;
                 s_b[et] = pre_b;
             }
-            int *counter = nullptr;
-            if constexpr (SK) if (!whole) {
-                // this tile's pieces: the pairs whose ranges meet its k-blocks
-                const int64_t u0 = static_cast<int64_t>(tile) * args.num_k;
-                const int q_lo = sk_owner(u0, sk_w, npairs);
-                const int q_hi = sk_owner(u0 + args.num_k - 1, sk_w, npairs);
-                counter = args.sk_counters + 2 * tile + static_cast<int>(rank);
-                if (et == 0) {
-                    // already every other piece in: this one finishes without storing
-                    sk_sh[0] = ld_acquire_gpu(counter) == q_hi - q_lo ? 1 : 0;
-                    int n = 0;
-                    for (int q = q_lo; q <= q_hi; ++q) {
-                        if (q == pair) continue;
-                        const int which = sk_start(q, sk_w, npairs) >= u0 ? 0 : 1;
-                        sk_sh[2 + n++] = (2 * q + which) * 2 + static_cast<int>(rank);
-                    }
-                    sk_sh[1] = n;
-                }
-            }
             if (!epi_sync(6)) break;
-            if (stager && nhave) fetch(ntile, pre_w, pre_b);
+            if (stager && tile + npairs < num_tiles) fetch(tile + npairs, pre_w, pre_b);
             const int row = m0 + quarter * 32 + lane;
             const float xs = (row < args.M && args.row_scale) ? __ldg(args.row_scale + row) : 1.f;
             if (!mbar_wait(TFULL(acc), aph, fault, 4)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN);
-            SkAdd sk{args.sk_partials, sk_sh + 2, 0, row_local};
-            bool finish = true;
-            if constexpr (SK) if (!whole) {
-                finish = sk_sh[0] != 0;
-                if (!finish) {
-                    // store this piece's partial sums, then count it in; the
-                    // piece whose count completes the tile finishes it
-                    const int which = sk_start(pair, sk_w, npairs) >= static_cast<int64_t>(tile) * args.num_k ? 0 : 1;
-                    int32_t *dst = args.sk_partials +
-                                   ((static_cast<size_t>(2 * pair + which) * 2 + rank) * 128 + row_local) * BN;
-                    sk_store_partial<EPI>(taddr, dst, col0, col1);
-                    __threadfence();
-                    if (!epi_sync(7)) break;
-                    if (et == 0) {
-                        __threadfence();
-                        // the last of the tile's pieces to count in finishes it
-                        sk_sh[0] = atomicAdd(counter, 1) == sk_sh[1] ? 1 : 0;
-                    }
-                    if (!epi_sync(8)) break;
-                    finish = sk_sh[0] != 0;
-                }
-                if (finish) {
-                    __threadfence();  // the other pieces' stores, seen through the counter
-                    sk.n = sk_sh[1];
-                }
-            }
-            if (finish)
-                epilogue_tile<EPI, SK>(args, tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
-                                       s_b, bufs, bsel, sk);
-            if (SK && !whole && finish && et == 0) *counter = 0;  // left zero for the next launch
+            epilogue_tile<EPI>(args, tmOut, taddr, m0, n0, quarter, col0, col1, lane, xs, s_ws,
+                               s_b, bufs, bsel);
             // hand the accumulator back to the leader's MMA issuer (one arrival per warp)
             tc_fence_before();
             __syncwarp();
@@ -753,11 +571,6 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             }
             acc ^= 1;
             if (acc == 0) aph ^= 1u;
-            it = nit;
-            tile = ntile;
-            kb0 = nkb0;
-            kb1 = nkb1;
-            have = nhave;
         }
         // the stores must have left shared memory before the CTA exits
         if (lane == 0) bulk_wait<0>();
@@ -824,9 +637,9 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, 
 // CTA pairs that can be resident at once for this kernel (cached per device;
 // launch_inst sets the shared-memory attribute on every launch, so a device
 // reset, which clears it, cannot leave a launch without it)
-template <int EPI, bool A_MN, bool B_MN, bool SK>
+template <int EPI, bool A_MN, bool B_MN>
 int resident_pairs(int dev) {
-    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN, SK>;
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     // atomic: first calls from several host threads may race to fill it (same value)
     static std::atomic<int> cached[32] = {};
     if (dev >= 0 && dev < 32) {
@@ -853,10 +666,10 @@ int resident_pairs(int dev) {
     return n;
 }
 
-template <int EPI, bool A_MN, bool B_MN, bool SK>
+template <int EPI, bool A_MN, bool B_MN>
 int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, const OutMaps &mo,
                 const GemmArgs &a, int pairs) {
-    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN, SK>;
+    auto kern = gemm_i8_kernel<EPI, A_MN, B_MN>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Cfg<EPI>::kSmemBytes)) != cudaSuccess)
         return launch_status("gemm (shared memory attribute)");
@@ -880,148 +693,21 @@ int launch_inst(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb, co
     return launch_status("gemm");
 }
 
-template <int EPI, bool A_MN, bool B_MN, bool SK>
-int launch_sized1(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
-                  const OutMaps &mo, const GemmArgs &a, int64_t max_pairs) {
+template <int EPI, bool A_MN, bool B_MN>
+int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
+                 const OutMaps &mo, const GemmArgs &a, int64_t tiles) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const int resident = resident_pairs<EPI, A_MN, B_MN, SK>(dev);
+    const int resident = resident_pairs<EPI, A_MN, B_MN>(dev);
     if (resident <= 0) {
         set_error("no CTA pair of the GEMM fits on the device");
         return 5;
     }
-    const int pairs = static_cast<int>(max_pairs < resident ? max_pairs : resident);
-    return launch_inst<EPI, A_MN, B_MN, SK>(s, ma, mb, mo, a, pairs);
-}
-// the data-parallel instance, or (a.sk, dequant / GEGLU epilogues only) the stream-K one
-template <int EPI, bool A_MN, bool B_MN>
-int launch_sized(cudaStream_t s, const CUtensorMap &ma, const CUtensorMap &mb,
-                 const OutMaps &mo, const GemmArgs &a, int64_t max_pairs) {
-    if constexpr (EPI == kEpiDequantBf16 || EPI == kEpiGegluBf16) {
-        if (a.sk) return launch_sized1<EPI, A_MN, B_MN, true>(s, ma, mb, mo, a, max_pairs);
-    }
-    return launch_sized1<EPI, A_MN, B_MN, false>(s, ma, mb, mo, a, max_pairs);
-}
-
-// resident CTA pairs of the stream-K kernel instance a call would launch
-int resident_for(int epi, bool a_mn, bool b_mn) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    switch (epi) {
-        case kEpiDequantBf16:
-            if (!a_mn && !b_mn) return resident_pairs<kEpiDequantBf16, false, false, true>(dev);
-            if (!a_mn && b_mn) return resident_pairs<kEpiDequantBf16, false, true, true>(dev);
-            if (a_mn && b_mn) return resident_pairs<kEpiDequantBf16, true, true, true>(dev);
-            break;
-        case kEpiGegluBf16:
-            return resident_pairs<kEpiGegluBf16, false, false, true>(dev);
-        default:
-            break;
-    }
-    return -1;
-}
-
-// The schedule of a call: the tile width, and whether stream-K runs (then on
-// how many pairs, with how many bytes of counters and partial sums).
-struct Plan {
-    int bn = BN;
-    int dp_bn = BN;  // the data-parallel width (what runs without stream-K)
-    bool sk = false;
-    int sk_pairs = 0;
-    int64_t counter_bytes = 0, workspace_bytes = 0;
-};
-constexpr int64_t kPartialBytes = 128 * BN * 4;  // one CTA half's accumulators
-int64_t align256_i(int64_t n) { return (n + 255) & ~int64_t(255); }
-
-Plan plan_gemm(const GemmCall &c) {
-    Plan p;
-    const bool geglu = c.epilogue == kEpiGegluBf16;
-    const bool wide = c.epilogue == kEpiDequantWide;
-    const int step = wide ? 64 : 32;  // the wide epilogue stores 64 columns at a time
-    const int64_t sms = num_sms() / 2;  // CTA pairs
-    const int64_t num_m = (c.M + 2 * BM - 1) / (2 * BM);
-    const int64_t kb = (c.K + BK - 1) / BK;
-    // Data parallel.  Tiles (256 rows x bn) are spread over the CTA pairs in
-    // waves (a persistent pair takes every P-th tile), so the critical path is
-    // ceil(tiles / P) tiles; a narrower tile can finish sooner when it fills
-    // the last wave better (N = 10240 at M = 2048: 320 tiles of 256 columns
-    // take 5 waves of 74 pairs, 368 tiles of 224 columns also 5 waves of
-    // slightly shorter tiles).  Only a K-major B is narrowed: an MN-major B
-    // tile is loaded as two 128-column boxes.
-    // Cost per tile k-block in "column" units: a tile's MMAs take nearly the
-    // same time at any width (measured on B200: a 128-wide tile ~0.91x the
-    // time of a 256-wide one), i.e. about kMmaFixed + bn.
-    constexpr int64_t kMmaFixed = 1170;
-    int64_t cost_dp = -1;
-    // XPUINT8_GEMM_BN=<128..256, multiple of 32> fixes the width (tests, tuning)
-    const char *force = std::getenv("XPUINT8_GEMM_BN");
-    const int forced = force ? std::atoi(force) : 0;
-    if (!geglu && !c.b_mn && forced >= 128 && forced <= BN && forced % step == 0) {
-        p.bn = forced;
-        cost_dp = 0;
-    } else if (!geglu && !c.b_mn) {
-        for (int cand = BN; cand >= 128; cand -= step) {
-            const int64_t tiles = num_m * ((c.N + cand - 1) / cand);
-            const int64_t cost = ((tiles + sms - 1) / sms) * kb * (kMmaFixed + cand);
-            if (cost_dp < 0 || cost < cost_dp) {
-                cost_dp = cost;
-                p.bn = cand;
-            }
-        }
-    } else {
-        const int64_t width = geglu ? 128 : BN;
-        const int64_t tiles = num_m * ((c.N + width - 1) / width);
-        cost_dp = ((tiles + sms - 1) / sms) * kb * (kMmaFixed + BN);
-    }
-    // Stream-K: the k-blocks of 256-wide tiles dealt evenly over the pairs.  A
-    // pair's range ends inside at most two tiles, whose partial sums cost about
-    // four k-blocks' time to store and read back.  Taken when it beats the
-    // data-parallel schedule by 10 %, on the dequant / GEGLU epilogues, with a
-    // workspace, and not when a tile width is forced.
-    p.dp_bn = p.bn;
-    // XPUINT8_GEMM_SCHEDULE=dp|sk forces the schedule where both are possible
-    // (tests run stream-K on shapes the cost model gives to data parallel)
-    const char *sched = std::getenv("XPUINT8_GEMM_SCHEDULE");
-    const bool force_dp = sched && std::strcmp(sched, "dp") == 0;
-    const bool force_sk = sched && std::strcmp(sched, "sk") == 0;
-    const bool sk_epi = c.epilogue == kEpiDequantBf16 || geglu;
-    if (sk_epi && c.sk_workspace && forced == 0 && kb >= 2 && cost_dp > 0 && !force_dp) {
-        const int64_t width = geglu ? 128 : BN;
-        const int64_t tiles = num_m * ((c.N + width - 1) / width);
-        const int resident = resident_for(c.epilogue, c.a_mn, c.b_mn);
-        // at most about five pieces per tile, and at least one k-block per pair
-        // (a pair with an empty range would count as a piece of a tile it
-        // never touches)
-        const int64_t pairs =
-            std::min<int64_t>(std::min<int64_t>(resident > 0 ? resident : sms, tiles * 4), tiles * kb);
-        const int64_t per_pair = (tiles * kb + pairs - 1) / pairs;
-        const int64_t cost_sk = (per_pair + 4) * (kMmaFixed + BN);
-        if (resident > 0 && (force_sk || 10 * cost_sk < 9 * cost_dp)) {
-            p.sk = true;
-            p.bn = BN;
-            p.sk_pairs = static_cast<int>(pairs);
-            p.counter_bytes = align256_i(tiles * 2 * 4);
-            p.workspace_bytes = p.counter_bytes + 2 * pairs * 2 * kPartialBytes;
-        }
-    }
-    return p;
+    const int pairs = static_cast<int>(tiles < resident ? tiles : resident);
+    return launch_inst<EPI, A_MN, B_MN>(s, ma, mb, mo, a, pairs);
 }
 
 }  // namespace
-
-int64_t gemm_workspace_bytes(const GemmCall &c) {
-    GemmCall probe = c;
-    probe.sk_workspace = reinterpret_cast<void *>(uintptr_t(256));  // "a workspace exists"
-    const Plan p = plan_gemm(probe);
-    return p.sk ? p.workspace_bytes : 0;
-}
-
-int64_t gemm_counter_bytes(const GemmCall &c) {
-    GemmCall probe = c;
-    probe.sk_workspace = reinterpret_cast<void *>(uintptr_t(256));
-    const Plan p = plan_gemm(probe);
-    return p.sk ? p.counter_bytes : 0;
-}
 
 int launch_gemm(cudaStream_t s, const GemmCall &c) {
     if (c.M <= 0 || c.N <= 0 || c.K <= 0) {
@@ -1060,13 +746,35 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("scales and bias need 16-byte aligned bases");
         return 2;
     }
-    Plan plan = plan_gemm(c);
-    if (plan.sk && (c.sk_workspace_bytes < plan.workspace_bytes ||
-                    (reinterpret_cast<uintptr_t>(c.sk_workspace) & 255u))) {
-        plan.sk = false;  // too small (or misaligned) a workspace: data parallel
-        plan.bn = plan.dp_bn;
+    // Output columns per tile.  Tiles (256 rows x bn) are spread over the CTA
+    // pairs in waves (a persistent pair takes every P-th tile, P = pairs on
+    // the device), so the critical path is ceil(tiles / P) tiles; a narrower
+    // tile can finish sooner when it fills the last wave better (N = 10240 at
+    // M = 2048: 320 tiles of 256 columns take 5 waves of 74 pairs, 368 tiles
+    // of 224 columns also 5 waves of 7/8 the work).  Each tile also costs a
+    // fixed drain and hand-over, counted as 32 columns.  Only a K-major B is
+    // narrowed: an MN-major B tile is loaded as two 128-column boxes.
+    int bn = BN;
+    const bool wide = c.epilogue == kEpiDequantWide;
+    const int step = wide ? 64 : 32;  // the wide epilogue stores 64 columns at a time
+    // XPUINT8_GEMM_BN=<128..256, multiple of 32> fixes the width (tests, tuning)
+    const char *force = std::getenv("XPUINT8_GEMM_BN");
+    const int forced = force ? std::atoi(force) : 0;
+    if (!geglu && !c.b_mn && forced >= 128 && forced <= BN && forced % step == 0) {
+        bn = forced;
+    } else if (!geglu && !c.b_mn) {
+        const int64_t sms = num_sms() / 2;  // CTA pairs
+        const int64_t num_m = (c.M + 2 * BM - 1) / (2 * BM);
+        int64_t best = -1;
+        for (int cand = BN; cand >= 128; cand -= step) {
+            const int64_t tiles = num_m * ((c.N + cand - 1) / cand);
+            const int64_t cost = ((tiles + sms - 1) / sms) * (cand + 32);
+            if (best < 0 || cost < best) {
+                best = cost;
+                bn = cand;
+            }
+        }
     }
-    const int bn = plan.bn;
     CUtensorMap ma, mb;
     // A: K-major [M rows, K bytes]; MN-major [K rows, M bytes]
     if (!c.a_mn) {
@@ -1100,7 +808,7 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
             if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 4, 16, 32, CU_TENSOR_MAP_DATA_TYPE_INT32,
                           CU_TENSOR_MAP_SWIZZLE_64B))
                 return 2;
-        } else if (c.epilogue == kEpiDequantWide) {
+        } else if (wide) {
             if (!make_map(&mo.m[i], base, c.N, c.M, c.ldo * 2, 64, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                           CU_TENSOR_MAP_SWIZZLE_128B))
                 return 2;
@@ -1126,32 +834,21 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("too many output tiles");
         return 2;
     }
-    int64_t max_pairs = tiles;
-    if (plan.sk) {
-        char *ws = static_cast<char *>(c.sk_workspace);
-        a.sk = 1;
-        a.sk_counters = reinterpret_cast<int *>(ws);
-        a.sk_partials = reinterpret_cast<int32_t *>(ws + plan.counter_bytes);
-        max_pairs = plan.sk_pairs;
-        if (!c.sk_zeroed && cudaMemsetAsync(ws, 0, static_cast<size_t>(plan.counter_bytes), s) !=
-                                cudaSuccess)
-            return launch_status("gemm (clearing the stream-K counters)");
-    }
     switch (c.epilogue) {
         case kEpiRawI32:
-            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiRawI32, false, false>(s, ma, mb, mo, a, max_pairs);
-            if (!c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, false, true>(s, ma, mb, mo, a, max_pairs);
-            if (c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, true, true>(s, ma, mb, mo, a, max_pairs);
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiRawI32, false, false>(s, ma, mb, mo, a, tiles);
+            if (!c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, false, true>(s, ma, mb, mo, a, tiles);
+            if (c.a_mn && c.b_mn) return launch_sized<kEpiRawI32, true, true>(s, ma, mb, mo, a, tiles);
             break;
         case kEpiDequantBf16:
-            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantBf16, false, false>(s, ma, mb, mo, a, max_pairs);
-            if (!c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, false, true>(s, ma, mb, mo, a, max_pairs);
-            if (c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, true, true>(s, ma, mb, mo, a, max_pairs);
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantBf16, false, false>(s, ma, mb, mo, a, tiles);
+            if (!c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, false, true>(s, ma, mb, mo, a, tiles);
+            if (c.a_mn && c.b_mn) return launch_sized<kEpiDequantBf16, true, true>(s, ma, mb, mo, a, tiles);
             break;
         case kEpiGegluBf16:
-            return launch_sized<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, max_pairs);
+            return launch_sized<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, tiles);
         case kEpiDequantWide:
-            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantWide, false, false>(s, ma, mb, mo, a, max_pairs);
+            if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantWide, false, false>(s, ma, mb, mo, a, tiles);
             break;
         default:
             break;

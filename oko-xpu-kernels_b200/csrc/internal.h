@@ -65,21 +65,8 @@ struct GemmCall {
     // this GEMM on the stream (the linear entries: that kernel is the
     // activation quantizer), so the GEMM may load them before waiting for it
     bool b_early = false;
-    // Stream-K workspace (may be null: the data-parallel schedule then runs).
-    // With enough bytes (gemm_workspace_bytes) the GEMM deals its k-blocks
-    // evenly over the CTA pairs when that beats whole tiles per pair.  Its
-    // first gemm_counter_bytes are arrival counters that must be zero when the
-    // kernel starts (every launch leaves them zero): sk_zeroed says the caller
-    // cleared them on the stream already, otherwise launch_gemm clears them.
-    void *sk_workspace = nullptr;
-    int64_t sk_workspace_bytes = 0;
-    bool sk_zeroed = false;
 };
 int launch_gemm(cudaStream_t s, const GemmCall &c);
-// bytes of stream-K workspace this call would use (0: it runs data-parallel),
-// and the leading part of it that holds the counters
-int64_t gemm_workspace_bytes(const GemmCall &c);
-int64_t gemm_counter_bytes(const GemmCall &c);
 int gemm_fault_status(int reset);  // device fault word of the GEMM waits
 
 // the bounded-wait self-test (waitprobe.cu): one CTA waits on an mbarrier that

@@ -72,8 +72,6 @@ def _signatures():
         "xpuint8_int_mm_dequant_stream": [vp] * 7 + [i64] * 3 + [i32, i64],
         "xpuint8_int_mm_geglu_stream": [vp] * 6 + [i64] * 3,
         "xpuint8_linear_stream": [vp] * 8 + [i64] * 3 + [i32],
-        "xpuint8_linear_workspace_bytes": [i64] * 3,
-        "xpuint8_linear_ws_stream": [vp] * 7 + [i64] * 3 + [i32],
         "xpuint8_linear_split_stream": [vp] * 6 + [i32, vp, vp] + [i64] * 3 + [i32],
         "xpuint8_ffn_workspace_bytes": [i64, i64, i64, i32],
         "xpuint8_ffn_stream": [vp] * 9 + [i64] * 3 + [i32],

@@ -576,15 +576,13 @@ def linear(x, w8, w_scale, bias=None, act: Optional[str] = None, residual=None,
     dev = x.device
     ws = expand_scale(w_scale, n, dev)
     b = None if bias is None else expand_scale(bias, n, dev)
-    # one workspace: the int8 activation, its row scales and, for shapes with
-    # few output tiles, the GEMM's stream-K area
-    work = torch.empty((lib.xpuint8_linear_workspace_bytes(m, n, k),), dtype=torch.uint8,
-                       device=dev)
+    xq = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     w8c = w8 if w8.is_contiguous() else w8.contiguous()
-    rc = lib.xpuint8_linear_ws_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws), _ptr(b),
-                                      _ptr(out), _ptr(work), m, n, k,
-                                      0 if act is None else ACTIVATIONS[act])
+    rc = lib.xpuint8_linear_stream(_stream(dev), _ptr(x2), _ptr(w8c), _ptr(ws), _ptr(b),
+                                   _ptr(out), _ptr(xq), _ptr(xs), m, n, k,
+                                   0 if act is None else ACTIVATIONS[act])
     if rc != 0:
         _err(lib, "linear")
     if residual is not None:

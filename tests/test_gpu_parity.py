@@ -361,22 +361,12 @@ def test_gemm_geglu_epilogue(m, inner, k):
     d = O.round_bf16((acc.astype(np.float32) * (bits(ws)[None, :] * bits(xs)[:, None]).astype(np.float32)).astype(np.float32))
     ref = O.f32_to_bf16_bits(O.activation(4, d[:, :inner], d[:, inner:]))
     got = bits(y)
-    # The device erf differs from the correctly rounded one in rare last bits,
-    # which can move the bf16 rounding of gelu(g) and so of y by one bf16 ulp
-    # (measured on B200: 42 of 384000 values, 1.1e-4); where 1 + erf(g/sqrt 2)
-    # cancels (g < -3) gelu(g) is tiny and its few significant bits may differ
-    # more, by a negligible absolute amount.  The gate: every difference is one
-    # ulp or below 1e-3 of the largest |y|, at most 5e-4 of the values differ,
-    # rel-L2 below 1e-3.
-    diff = got != ref
-    ulps = np.abs(got.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32))
-    gf, rf = O.bf16_bits_to_f32(got), O.bf16_bits_to_f32(ref)
-    tiny = np.abs(gf - rf) <= 1e-3 * np.abs(rf).max()
-    print(f"\nGEGLU epilogue {m}x{inner}x{k}: {int(diff.sum())} of {got.size} bf16 values "
-          f"differ (rate {diff.mean():.2e}; {int((diff & (ulps > 1)).sum())} by more than one "
-          f"ulp, all below 1e-3 of max|y|), rel-L2 {rel_l2(got, ref):.2e}")
-    assert np.all((ulps <= 1) | tiny)
-    assert diff.mean() < 5e-4
+    # the device erf differs from the correctly rounded one in rare last bits,
+    # which can move a bf16 rounding: at most 1e-4 of the values
+    diff = int((got != ref).sum())
+    print(f"\nGEGLU epilogue {m}x{inner}x{k}: {diff} of {got.size} bf16 values differ "
+          f"(rate {diff / got.size:.2e})")
+    assert diff / got.size < CODE_RATE
     assert rel_l2(got, ref) < 1e-3
 
 
@@ -767,98 +757,3 @@ def test_split_projection_rejects_bad_parts():
         int8.linear_split(x, w8, ws, parts=3)      # 48 columns: not a multiple of 32
     with pytest.raises(ValueError):
         int8.linear_split(x, w8, ws, parts=5)      # 144 rows do not split in 5
-
-
-# ------------------------------------------------------------------------ stream-K schedule
-
-def _dp_linear(x, w8, ws, bias):
-    """The linear through the data-parallel entry (no workspace: whole tiles per pair)."""
-    from xpu_kernels.int8 import _lib as L
-    lib = L.load()
-    m, k = x.shape
-    n = w8.shape[0]
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
-    xq = torch.empty((m, k), dtype=torch.int8, device=DEV)
-    xs = torch.empty((m,), dtype=torch.float32, device=DEV)
-    rc = lib.xpuint8_linear_stream(L._stream(out.device), L._ptr(x), L._ptr(w8), L._ptr(ws),
-                                   L._ptr(bias), L._ptr(out), L._ptr(xq), L._ptr(xs), m, n, k, 0)
-    assert rc == 0, lib.xpuint8_last_error()
-    return out
-
-
-def _sk_planned(m, n, k):
-    from xpu_kernels.int8 import _lib as L
-    lib = L.load()
-    base = ((m * k + 255) // 256) * 256 + ((m * 4 + 255) // 256) * 256
-    return lib.xpuint8_linear_workspace_bytes(m, n, k) > base
-
-
-@pytest.mark.parametrize("m,n,k,force", [
-    (2048, 1280, 1280, None), (2048, 1280, 5120, None), (4096, 1280, 5120, None),
-    (300, 1040, 1280, "sk"), (2048, 10240, 1280, "sk"), (77, 272, 4096, "sk"),
-    (1, 64, 1024, "sk"), (5000, 160, 2560, "sk")])
-def test_stream_k_linear_is_bit_exact(monkeypatch, m, n, k, force):
-    """The stream-K schedule (k-blocks dealt evenly over the CTA pairs, split
-    tiles summed from int32 partials) gives the data-parallel schedule's bits,
-    on the shapes the cost model sends to it (N = 1280) and, forced, on ragged
-    and large-N shapes; and the oracle's on sampled rows."""
-    from xpu_kernels import int8
-    if force:
-        monkeypatch.setenv("XPUINT8_GEMM_SCHEDULE", force)
-    else:
-        assert _sk_planned(m, n, k), "the cost model should pick stream-K for this shape"
-    x = rand_bf16((m, k), 300 + m, outliers=4).to(DEV)
-    _, w8n, wsn = _prep(n, k, 301 + n)
-    w8, ws = torch.from_numpy(w8n).to(DEV), torch.from_numpy(wsn).to(DEV)
-    bias = (torch.randn(n, generator=torch.Generator().manual_seed(k)) * 0.01).to(DEV)
-    got = int8.linear(x, w8, ws, bias)
-    monkeypatch.setenv("XPUINT8_GEMM_SCHEDULE", "dp")
-    ref = _dp_linear(x, w8, ws, bias)
-    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
-    rows = np.unique(np.linspace(0, m - 1, 9).astype(int))
-    assert np.array_equal(bits(got)[rows], O.linear(bits(x)[rows], w8n, wsn, bits(bias)))
-
-
-def test_stream_k_workspace_needs_no_initialisation():
-    """The linear's workspace may hold anything: the call clears its stream-K
-    counters; two calls in a row on one workspace give the same bits."""
-    from xpu_kernels import int8
-    from xpu_kernels.int8 import _lib as L
-    lib = L.load()
-    m, n, k = 2048, 1280, 5120
-    assert _sk_planned(m, n, k)
-    x = rand_bf16((m, k), 310).to(DEV)
-    _, w8n, wsn = _prep(n, k, 311)
-    w8, ws = torch.from_numpy(w8n).to(DEV), torch.from_numpy(wsn).to(DEV)
-    ref = int8.linear(x, w8, ws)
-    work = torch.full((lib.xpuint8_linear_workspace_bytes(m, n, k),), 0x7F, dtype=torch.uint8,
-                      device=DEV)
-    for _ in range(2):
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
-        rc = lib.xpuint8_linear_ws_stream(L._stream(out.device), L._ptr(x), L._ptr(w8), L._ptr(ws),
-                                          None, L._ptr(out), L._ptr(work), m, n, k, 0)
-        assert rc == 0, lib.xpuint8_last_error()
-        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
-
-
-@pytest.mark.parametrize("act", ["geglu_erf", "gelu_erf"])
-def test_stream_k_ffn_and_backward_match_data_parallel(monkeypatch, act):
-    """The FFN (GEGLU up-projection epilogue and the down-projection) and the
-    int8 backward (dx with an MN-major B, dW with both operands MN-major) give
-    the same bits under either schedule."""
-    from xpu_kernels import int8
-    m, k, inner = 1024, 1280, 2560
-    n_up = 2 * inner if act in int8.PAIRED_ACTIVATIONS else inner
-    x = rand_bf16((m, k), 320).to(DEV)
-    up8, up_s = (torch.from_numpy(t).to(DEV) for t in _prep(n_up, k, 321)[1:])
-    dn8, dn_s = (torch.from_numpy(t).to(DEV) for t in _prep(k, inner, 322)[1:])
-    dy = rand_bf16((m, k), 323, scale=1e-3).to(DEV)
-    xq, xs = int8.quantize(x)
-    res = {}
-    for sched in ("sk", "dp"):
-        monkeypatch.setenv("XPUINT8_GEMM_SCHEDULE", sched)
-        res[sched] = (int8.ffn(x, up8, up_s, dn8, dn_s, act=act),
-                      int8.linear_dx_int8(dy, dn8, dn_s),
-                      int8.linear_dw_int8(dy, xq, xs))
-    for a, b in zip(res["sk"], res["dp"]):
-        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
