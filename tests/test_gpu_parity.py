@@ -117,6 +117,20 @@ def test_quantize_is_bit_exact(m, k):
     assert np.array_equal(bits(q), qr)
 
 
+@pytest.mark.parametrize("k", [1024, 2048, 3072, 4096, 5120, 6144, 7168, 8192])
+@pytest.mark.parametrize("m", [1, 3, 333])
+def test_quantize_four_group_teams_are_bit_exact(m, k):
+    """Row widths that are multiples of 1024 run the four-groups-per-slot
+    quantizer (teams of 4 to 14 slots, 1 to 4 rows per batch); ragged row
+    counts leave partial last batches.  Codes and scales equal the oracle's."""
+    from xpu_kernels import int8
+    x = rand_bf16((m, k), 90 + k + m, outliers=6)
+    q, s = int8.quantize(x.to(DEV))
+    qr, sr = O.convrot_quantize(bits(x))
+    assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
+    assert np.array_equal(bits(q), qr)
+
+
 def test_quantize_edge_rows():
     from xpu_kernels import int8
     x = torch.zeros(6, 512, dtype=torch.bfloat16)
