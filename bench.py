@@ -69,6 +69,21 @@ WORKLOAD = ("linear(x bf16 [2048,1280]) -> rotate+quantize -> tcgen05 int8 GEMM 
             "dequant -> bf16 [2048,10240] (config C3 W1, SDXL GEGLU up-projection)")
 
 
+class _stdout_to_stderr:
+    """File descriptor 1 pointed at stderr for the duration (C libraries included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
 def _dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -263,8 +278,12 @@ def run_gpu(args):
         import datetime
         import torch.distributed as dist
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        # NCCL may print its version on stdout while it sets up the
+        # communicator; stdout carries only the result line
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=dev)
+            dist.barrier()
     lib = L._lib()
     stream = torch.cuda.current_stream(dev)
 
@@ -721,7 +740,9 @@ def run_nshard(args):
     dev = torch.device("cuda", local)
     if ws_ > 1:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
     m, k, n = args.nshard_m, 4096, 14336
     g = torch.Generator(device=dev).manual_seed(4)
     x = torch.randn(m, k, generator=g, device=dev)
