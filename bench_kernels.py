@@ -85,7 +85,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "gemm_raw", "gemm_nn", "gemm_tn", "geglu",
                                      "rotate_quant", "rotate", "linear", "ffn", "dx", "dw",
-                                     "quantize_row", "dequant", "dequant_act"])
+                                     "quantize_row", "colquant", "dequant", "dequant_act"])
     ap.add_argument("--M", type=int, default=2048)
     ap.add_argument("--N", type=int, default=10240)
     ap.add_argument("--K", type=int, default=1280)
@@ -150,6 +150,20 @@ def main(argv=None):
                 rc = lib.xpuint8_quantize_row_stream(_stream(dev), _ptr(X[j]), None, _ptr(Q[j]), _ptr(sc[j]), M, K)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = (4 * M * K) if a.case == "rotate" else (3 * M * K + 4 * M)
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9, "bytes": nbytes}
+    elif a.case == "colquant":
+        DY = [bf(M, N, s=1e-3) for _ in range(S)]
+        GQ = [torch.empty(M, N, dtype=torch.int8, device=dev) for _ in range(S)]
+        TG = [torch.empty(N, dtype=torch.float32, device=dev) for _ in range(S)]
+        xs = f32(M)
+
+        def fn(i):
+            j = i % S
+            rc = lib.xpuint8_colquant_stream(_stream(dev), _ptr(DY[j]), _ptr(xs), _ptr(GQ[j]),
+                                             _ptr(TG[j]), M, N)
+            assert rc == 0, lib.xpuint8_last_error()
+        nbytes = 3 * M * N + 4 * M + 4 * N
         t = _time(fn, a.iters, st)
         res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9, "bytes": nbytes}
     elif a.case == "dequant":

@@ -198,7 +198,9 @@ constexpr int kColRows = 128;
 
 // column abs-max of g = dy * xs: a CTA reduces its tile over rows in shared
 // memory and posts one atomicMax per column (on the bit pattern of a
-// non-negative float)
+// non-negative float).  dy is read with the normal L2 policy: the second pass
+// (colquant_kernel) reads it again, from L2 when it fits (the C4 gradient,
+// 42 MB, does), and streams it out of the cache there.
 __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict__ dy,
                                                       const float *__restrict__ xs,
                                                       unsigned int *__restrict__ amax,
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict
 #pragma unroll 8
         for (int64_t m = m0 + ty; m < m1; m += 8) {
             const float x = __ldg(xs + m);
-            const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
+            const uint4 w = __ldcg(reinterpret_cast<const uint4 *>(dy + m * N + n));
             const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
