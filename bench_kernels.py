@@ -85,7 +85,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "gemm_raw", "gemm_nn", "gemm_tn", "geglu",
                                      "rotate_quant", "rotate", "linear", "ffn", "dx", "dw",
-                                     "quantize_row", "colquant", "dequant", "dequant_act"])
+                                     "quantize_row", "colquant", "rope", "dequant", "dequant_act"])
     ap.add_argument("--M", type=int, default=2048)
     ap.add_argument("--N", type=int, default=10240)
     ap.add_argument("--K", type=int, default=1280)
@@ -164,6 +164,24 @@ def main(argv=None):
                                              _ptr(TG[j]), M, N)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = 3 * M * N + 4 * M + 4 * N
+        t = _time(fn, a.iters, st)
+        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9, "bytes": nbytes}
+    elif a.case == "rope":
+        # M rows (B=1, S=M) of N // 128 heads of D=128 from an int32 [M, 3N] qkv accumulator
+        H, D = N // 128, 128
+        ACC = [torch.randint(-2 ** 20, 2 ** 20, (M, 3 * N), generator=g, device=dev, dtype=torch.int32)
+               for _ in range(S)]
+        xs, ws, wt = f32(M), f32(3 * N), torch.ones(D, device=dev)
+        ang = torch.rand(1, M, 1, D // 2, generator=g, device=dev) * 3.0
+        pe = torch.stack([torch.stack([ang.cos(), -ang.sin()], -1),
+                          torch.stack([ang.sin(), ang.cos()], -1)], -2)
+
+        def fn(i):
+            a3 = ACC[i % S].view(1, M, 3 * N)
+            ops.rms_rope_split_half_dequant(a3[:, :, :N].unflatten(-1, (H, D)),
+                                            a3[:, :, N:2 * N].unflatten(-1, (H, D)), pe,
+                                            ws[:N], ws[N:2 * N], xs, wt)
+        nbytes = 2 * (4 * M * N + 2 * M * N)
         t = _time(fn, a.iters, st)
         res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9, "bytes": nbytes}
     elif a.case == "dequant":

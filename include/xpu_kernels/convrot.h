@@ -151,6 +151,23 @@ int xpuint8_linear_split_stream(const void *stream, const void *x, const int8_t 
                                 int32_t nparts, int8_t *xq, float *xs, int64_t M, int64_t N,
                                 int64_t K, int32_t activation);
 
+/* RMS norm + rotary embedding of attention heads, B x S rows of H heads of
+ * D elements (D 64, 128 or 256): x is bf16 (x_is_int32 = 0) or the INT8 GEMM's
+ * int32 accumulator (x_is_int32 = 1: first dequantized as bf16(float(acc) *
+ * (w_scale[h*D+d] * x_scale[row])), w_scale [H*D], x_scale [B*S]); per head
+ * y = bf16((x * rsqrt(mean(x^2) + eps)) * weight) (weight [D]), then each pair
+ * (d, d + D/2) (split_half) or (2i, 2i+1) rotated by freqs [freqs_batch,
+ * freqs_seq, D/2, 2, 2] fp32 ([[cos, -sin], [sin, cos]]; 1 broadcasts) into
+ * out bf16.  ldx / ldo: elements between rows (an accumulator slice of a fused
+ * qkv GEMM has ldx = 3 * H * D).  Replaces python/xpu_kernels/triton/rope.py
+ * :360-408 (_rows, _rows_dq) behind rms_rope_split_half(_dequant) (:643-652,
+ * :694), the chain of triton/reference.py:63-98. */
+int xpuint8_rms_rope_stream(const void *stream, const void *x, int32_t x_is_int32, int64_t ldx,
+                            const float *x_scale, const float *w_scale, const float *weight,
+                            const float *freqs, int64_t freqs_batch, int64_t freqs_seq, void *out,
+                            int64_t ldo, int64_t B, int64_t S, int64_t H, int64_t D, float eps,
+                            int32_t split_half);
+
 /* The fused FFN down(act(up(x))) (ops.py:649-719) in one C call; activation 3
  * situ, 4 GEGLU (fused into the up-projection's epilogue), 5 GELU-erf.
  * `workspace` holds xpuint8_ffn_workspace_bytes(M, K, inner, activation)

@@ -631,6 +631,40 @@ int xpuint8_colquant_stream(const void *stream, const void *dy, const float *x_s
     return launch_colquant(as_stream(stream), dy, x_scale, gq, tg, M, N);
 }
 
+int xpuint8_rms_rope_stream(const void *stream, const void *x, int32_t x_is_int32, int64_t ldx,
+                            const float *x_scale, const float *w_scale, const float *weight,
+                            const float *freqs, int64_t freqs_batch, int64_t freqs_seq, void *out,
+                            int64_t ldo, int64_t B, int64_t S, int64_t H, int64_t D, float eps,
+                            int32_t split_half) {
+    if (B <= 0 || S <= 0 || H <= 0) {
+        set_error("rms_rope: B, S and H must be positive");
+        return 2;
+    }
+    if (D != 64 && D != 128 && D != 256) {
+        set_error("rms_rope: the head dim must be 64, 128 or 256");
+        return 2;
+    }
+    if (ldx < H * D || ldo < H * D) {
+        set_error("rms_rope: row strides must be at least H * D elements");
+        return 2;
+    }
+    if ((freqs_batch != 1 && freqs_batch != B) || (freqs_seq != 1 && freqs_seq != S)) {
+        set_error("rms_rope: freqs must be [1 or B, 1 or S, D/2, 2, 2]");
+        return 2;
+    }
+    if (!x || !weight || !freqs || !out || (x_is_int32 && (!x_scale || !w_scale))) {
+        set_error("a required pointer is null");
+        return 2;
+    }
+    if (!aligned16(freqs) || (reinterpret_cast<uintptr_t>(x) & (x_is_int32 ? 3u : 1u)) ||
+        (reinterpret_cast<uintptr_t>(out) & 1u)) {
+        set_error("rms_rope: freqs must be 16-byte aligned, x and out aligned to their element size");
+        return 2;
+    }
+    return launch_rms_rope(as_stream(stream), x, x_is_int32 != 0, ldx, x_scale, w_scale, weight, freqs,
+                           freqs_batch, freqs_seq, out, ldo, B, S, H, D, eps, split_half != 0);
+}
+
 int xpuint8_fault_status(int32_t reset) {
     const int g = gemm_fault_status(reset);
     const int r = probe_fault_status(reset);

@@ -69,6 +69,13 @@ struct GemmCall {
 int launch_gemm(cudaStream_t s, const GemmCall &c);
 int gemm_fault_status(int reset);  // device fault word of the GEMM waits
 
+// RMS norm + rotary embedding of attention heads (rope.cu), from bf16 heads or
+// from the int32 accumulator with its dequant
+int launch_rms_rope(cudaStream_t s, const void *in, bool in_int32, int64_t ld_in, const float *x_scale,
+                    const float *w_scale, const float *weight, const float *freqs, int64_t fb,
+                    int64_t fs, void *out, int64_t ld_out, int64_t B, int64_t S, int64_t H, int64_t D,
+                    float eps, bool split_half);
+
 // the bounded-wait self-test (waitprobe.cu): one CTA waits on an mbarrier that
 // nothing arrives on, gives up after limit_ns and records `site`
 int launch_wait_probe(int64_t limit_ns, int site, int64_t *elapsed_ns);

@@ -33,6 +33,10 @@ from .int8 import (
     linear,
     linear_acc,
     linear_split,
+    rms_rope,
+    rms_rope_dequant,
+    rms_rope_split_half,
+    rms_rope_split_half_dequant,
     linear_dw,
     linear_dw_int8,
     linear_dx,
@@ -62,7 +66,8 @@ __all__ = [
     "ACTIVATIONS", "Int8Linear", "PAIRED_ACTIVATIONS", "TrainableInt8Linear", "available",
     "capture_status", "dequant", "dequant_act_quantize", "dequant_slice", "dequant_weight",
     "dequant_weight_torch", "device_name", "expand_scale", "ffn", "ffn_situ", "int8_linear",
-    "int_mm", "is_capturing", "linear", "linear_acc", "linear_split", "linear_dw", "linear_dw_int8",
+    "int_mm", "is_capturing", "linear", "linear_acc", "linear_split", "rms_rope", "rms_rope_dequant", "rms_rope_split_half",
+    "rms_rope_split_half_dequant", "linear_dw", "linear_dw_int8",
     "linear_dx", "linear_dx_int8", "load", "prepare_for_capture", "prepare_weight",
     "prepare_weight_fused", "quantize", "quantize_act", "quantize_row", "quantize_row_torch",
     "require_capture_ready", "rotate", "selftest", "unsupported_reason", "int8",

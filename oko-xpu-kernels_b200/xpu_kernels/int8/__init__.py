@@ -40,6 +40,10 @@ from .ops import (
     linear,
     linear_acc,
     linear_split,
+    rms_rope,
+    rms_rope_dequant,
+    rms_rope_split_half,
+    rms_rope_split_half_dequant,
     linear_dw,
     linear_dw_int8,
     linear_dx,
@@ -59,7 +63,8 @@ __all__ = [
     "ACTIVATIONS", "Int8Linear", "PAIRED_ACTIVATIONS", "TrainableInt8Linear", "available",
     "dequant", "dequant_act_quantize", "dequant_slice", "dequant_weight",
     "dequant_weight_torch", "device_name", "expand_scale", "ffn", "ffn_situ", "int8_linear",
-    "int_mm", "linear", "linear_acc", "linear_split", "linear_dw", "linear_dw_int8", "linear_dx",
+    "int_mm", "linear", "linear_acc", "linear_split", "rms_rope", "rms_rope_dequant", "rms_rope_split_half",
+    "rms_rope_split_half_dequant", "linear_dw", "linear_dw_int8", "linear_dx",
     "linear_dx_int8", "load", "prepare_weight", "prepare_weight_fused", "quantize",
     "quantize_act", "quantize_row", "quantize_row_torch", "rotate", "selftest",
     "unsupported_reason",

@@ -81,6 +81,8 @@ def _signatures():
         "xpuint8_linear_dx_int8_stream": [vp] * 6 + [i64] * 3,
         "xpuint8_linear_dw_int8_workspace_bytes": [i64] * 3,
         "xpuint8_linear_dw_int8_stream": [vp] * 6 + [i64] * 3,
+        "xpuint8_rms_rope_stream": [vp, vp, i32, i64] + [vp] * 4 + [i64, i64, vp] + [i64] * 5
+                                   + [ctypes.c_float, i32],
         "xpuint8_fault_status": [i32],
         "xpuint8_wait_probe": [i64, i32, vp],
         "xpuint8_check_scale_math": [vp, vp],

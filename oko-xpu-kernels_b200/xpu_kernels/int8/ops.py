@@ -640,6 +640,99 @@ def linear_split(x, w8, w_scale, bias=None, parts: int = 3, act: Optional[str] =
     return tuple(o.reshape(*x.shape[:-1], n) for o in outs)
 
 
+def _rope_rows(x, what):
+    """(row stride, B, S, H, D) of a [B, S, H, D] view whose heads are
+    contiguous within a row and whose rows are uniformly strided (a slice of a
+    fused qkv tensor qualifies)."""
+    if x.dim() != 4:
+        raise ValueError(f"{what} must be [B, S, H, D], got {tuple(x.shape)}")
+    B, S, H, D = x.shape
+    st = x.stride()
+    if st[3] != 1 or st[2] != D or (B > 1 and st[0] != S * st[1]):
+        raise ValueError(f"{what}: the heads of a row must be contiguous and the rows "
+                         f"uniformly strided (strides {st})")
+    return st[1], B, S, H, D
+
+
+def _rope_freqs(freqs_cis, B, S, D, dev):
+    f = freqs_cis
+    if f.dim() == 6:              # [B or 1, S or 1, 1, D/2, 2, 2]
+        f = f.squeeze(2)
+    if f.dim() != 5 or f.shape[2:] != (D // 2, 2, 2) or f.shape[0] not in (1, B) or \
+            f.shape[1] not in (1, S):
+        raise ValueError(f"freqs_cis must be [1|B, 1|S, 1, D/2, 2, 2], got {tuple(freqs_cis.shape)}")
+    return f.to(device=dev, dtype=torch.float32).contiguous()
+
+
+def _rms_rope(x, freqs_cis, scale, epsilon, split_half, x_scale=None, w_scale=None):
+    lib = _lib()
+    is_acc = x_scale is not None
+    if is_acc and x.dtype != torch.int32:
+        raise TypeError("the accumulator must be int32")
+    if not is_acc and x.dtype != torch.bfloat16:
+        raise TypeError("x must be bfloat16")
+    ld, B, S, H, D = _rope_rows(x, "x")
+    dev = x.device
+    f = _rope_freqs(freqs_cis, B, S, D, dev)
+    w = scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    if w.numel() != D:
+        raise ValueError(f"scale must have {D} elements")
+    xs = ws = None
+    if is_acc:
+        xs = x_scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+        ws = w_scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+        if xs.numel() != B * S or ws.numel() != H * D:
+            raise ValueError("x_scale must have B*S elements and w_scale H*D")
+    out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dev)
+    rc = lib.xpuint8_rms_rope_stream(_stream(dev), ctypes.c_void_p(x.data_ptr()), 1 if is_acc else 0,
+                                     ld, _ptr(xs), _ptr(ws), _ptr(w), _ptr(f), f.shape[0], f.shape[1],
+                                     _ptr(out), H * D, B, S, H, D, float(epsilon),
+                                     1 if split_half else 0)
+    if rc != 0:
+        _err(lib, "rms_rope")
+    return out
+
+
+def rms_rope(x, freqs_cis, scale, epsilon=1e-6, split_half=True):
+    """RMS norm (with the per-dim ``scale``) then rotary embedding of attention
+    heads, bf16 ``[B, S, H, D]`` -> bf16 (triton/rope.py:360-376 ``_rows``; the
+    chain ``rope_split_half(rms_norm(x, scale, eps), freqs_cis)`` of
+    triton/reference.py:63-98).  ``freqs_cis`` is ``[1|B, 1|S, 1, D/2, 2, 2]``
+    holding ``[[cos, -sin], [sin, cos]]`` per pair; ``split_half`` rotates
+    ``(d, d + D/2)``, otherwise ``(2i, 2i + 1)``.  D is 64, 128 or 256."""
+    return _rms_rope(x, freqs_cis, scale, epsilon, split_half)
+
+
+def rms_rope_dequant(acc, freqs_cis, scale, x_scale, w_scale, epsilon=1e-6, split_half=True):
+    """:func:`rms_rope` reading the INT8 GEMM's int32 accumulator (a
+    ``[B, S, H, D]`` view, e.g. a slice of the fused qkv accumulator) with the
+    dequant folded into the load: ``bf16(float(acc) * (w_scale * x_scale))``
+    (triton/rope.py:378-408 ``_rows_dq``).  ``x_scale`` is ``[B, S]`` or
+    ``[B*S]``, ``w_scale`` the slice's ``[H*D]`` column scales."""
+    return _rms_rope(acc, freqs_cis, scale, epsilon, split_half, x_scale, w_scale)
+
+
+def rms_rope_split_half(q, k, freqs_cis, q_scale, k_scale=None, epsilon=1e-6):
+    """``(rms_rope(q), rms_rope(k))`` with split-half rotation
+    (triton/rope.py:694)."""
+    if k_scale is None:
+        k_scale = q_scale
+    return (rms_rope(q, freqs_cis, q_scale, epsilon), rms_rope(k, freqs_cis, k_scale, epsilon))
+
+
+def rms_rope_split_half_dequant(q_acc, k_acc, freqs_cis, q_w, k_w, x_scale, q_scale,
+                                k_scale=None, epsilon=1e-6, split_half=True):
+    """The q and k slices of a fused qkv accumulator through
+    :func:`rms_rope_dequant` (triton/rope.py:643-652: ``q_w`` / ``k_w`` are
+    the slices' column scales, ``q_scale`` / ``k_scale`` the norms')."""
+    if k_scale is None:
+        k_scale = q_scale
+    if k_w is None:
+        k_w = q_w
+    return (rms_rope_dequant(q_acc, freqs_cis, q_scale, x_scale, q_w, epsilon, split_half),
+            rms_rope_dequant(k_acc, freqs_cis, k_scale, x_scale, k_w, epsilon, split_half))
+
+
 def ffn(x, up_w8, up_scale, down_w8, down_scale, down_bias=None, act="situ"):
     """``act(up(x)) @ down.T`` with the bf16 [M, 2*ffn] intermediate never
     written (ops.py:649-719).

@@ -43,7 +43,7 @@ __all__ = [
     "convrot_quantize", "dequant_epilogue", "dequant_act_quantize",
     "dequant_weight", "prepare_weight", "prepare_weight_fused", "quantize_row",
     "int_mm", "linear", "linear_acc", "ffn", "linear_dx_int8", "linear_dw",
-    "linear_dw_int8", "colquant_scaled", "convrot_linear_reference",
+    "linear_dw_int8", "colquant_scaled", "convrot_linear_reference", "rms_rope",
 ]
 
 GROUP = 256
@@ -506,4 +506,55 @@ def convrot_linear_reference(x, w8, w_scale, bias=None, rotation: str = "hadamar
     out = round_bf16(r)
     if bias is not None:
         out = round_bf16((out + round_bf16(np.asarray(bias, dtype=np.float32).reshape(1, -1))).astype(np.float32))
+    return f32_to_bf16_bits(out)
+
+
+# ---------------------------------------------------------------------------
+# the int32-accumulator consumer of the fused qkv projection
+# ---------------------------------------------------------------------------
+
+def rms_rope(x, freqs, weight, eps: float = 1e-6, split_half: bool = True,
+             x_scale=None, w_scale=None):
+    """RMS norm + rotary embedding per head (python/xpu_kernels/triton/rope.py
+    :378-408 ``_rows_dq`` and :360-376 ``_rows``; the torch chain they restate,
+    triton/reference.py:63-98).
+
+    ``x``: bf16 bits ``[B, S, H, D]``, or int32 ``[B, S, H, D]`` with
+    ``x_scale [B*S]`` and ``w_scale [H*D]`` (then first
+    ``bf16(float(acc) * (w_scale * x_scale))``, rope.py:398-401).  Per head:
+    ``inv = rsqrt(mean(x^2) + eps)``, ``y = bf16((x * inv) * weight)``, then the
+    pairs ``(d, d + D/2)`` (split half) or ``(2i, 2i + 1)`` rotated by
+    ``freqs [fb, fs, D/2, 2, 2]`` (fp32; size-1 leading dims broadcast):
+    ``out = bf16(f00 y_a + f01 y_b)``, ``bf16(f10 y_a + f11 y_b)``, every
+    product and sum rounded in fp32.  The mean of squares is summed in float64
+    and rounded (the kernels' own summation orders differ from each other in
+    the last bit; the tests' tolerance covers it).  Returns bf16 bits."""
+    if x_scale is not None:
+        acc = np.asarray(x, dtype=np.int32)
+        B, S, H, D = acc.shape
+        xs = np.asarray(x_scale, dtype=np.float32).reshape(B, S, 1, 1)
+        ws = np.asarray(w_scale, dtype=np.float32).reshape(1, 1, H, D)
+        xf = round_bf16((acc.astype(np.float32) * (ws * xs).astype(np.float32)).astype(np.float32))
+    else:
+        xf = bf16_bits_to_f32(as_bf16_bits(x))
+        B, S, H, D = xf.shape
+    ss = (xf.astype(np.float64) ** 2).sum(axis=-1, keepdims=True).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(((ss / np.float32(D)).astype(np.float32)
+                                      + np.float32(eps)).astype(np.float64))).astype(np.float32)
+    wt = np.asarray(weight, dtype=np.float32).reshape(1, 1, 1, D)
+    y = round_bf16(((xf * inv).astype(np.float32) * wt).astype(np.float32))
+    f = np.asarray(freqs, dtype=np.float32)
+    f = np.broadcast_to(f.reshape(f.shape[0], f.shape[1], 1, D // 2, 2, 2), (B, S, 1, D // 2, 2, 2))
+    if split_half:
+        ya, yb = y[..., :D // 2], y[..., D // 2:]
+    else:
+        ya, yb = y[..., 0::2], y[..., 1::2]
+    f00, f01, f10, f11 = f[..., 0, 0], f[..., 0, 1], f[..., 1, 0], f[..., 1, 1]
+    oa = ((f00 * ya).astype(np.float32) + (f01 * yb).astype(np.float32)).astype(np.float32)
+    ob = ((f10 * ya).astype(np.float32) + (f11 * yb).astype(np.float32)).astype(np.float32)
+    out = np.empty_like(y)
+    if split_half:
+        out[..., :D // 2], out[..., D // 2:] = oa, ob
+    else:
+        out[..., 0::2], out[..., 1::2] = oa, ob
     return f32_to_bf16_bits(out)

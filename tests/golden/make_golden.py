@@ -135,6 +135,38 @@ def main() -> None:
 
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays, torch {torch.__version__}")
+    _rope_fixture(args.reference, os.path.join(os.path.dirname(args.out), "reference_rope.npz"))
+
+
+def _rope_fixture(reference: str, path: str) -> None:
+    """The consumer of the fused qkv accumulator: the reference's torch chain
+    (python/xpu_kernels/triton/reference.py:63-98, ``rms_rope_split_half``)
+    run on the bf16 dequant of an int32 accumulator slice, exactly as its
+    probe builds the expected value (triton/rope.py:484-521)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "ref_triton_reference", os.path.join(reference, "python", "xpu_kernels", "triton", "reference.py"))
+    tref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tref)
+    g = torch.Generator().manual_seed(77)
+    B, S, H, D = 1, 48, 3, 128
+    M, C = B * S, 3 * H * D
+    acc = torch.randint(-(2 ** 23), 2 ** 23, (M, C), generator=g, dtype=torch.int32)
+    xs = torch.rand(M, generator=g) * 0.02 + 0.001
+    ws = torch.rand(C, generator=g) * 0.02 + 0.001
+    scale = torch.rand(D, generator=g) * 0.2 + 0.9
+    ang = torch.rand(B, S, 1, D // 2, generator=g) * 3.0
+    pe = torch.stack([torch.stack([ang.cos(), -ang.sin()], -1),
+                      torch.stack([ang.sin(), ang.cos()], -1)], -2)
+    out = {"acc": _bits(acc), "xs": _bits(xs), "ws": _bits(ws), "scale": _bits(scale),
+           "pe": _bits(pe.contiguous())}
+    for name, lo in (("q", 0), ("k", H * D)):
+        x = (acc[:, lo:lo + H * D].to(torch.float32) * (ws[lo:lo + H * D] * xs[:, None])
+             ).to(torch.bfloat16).view(B, S, H, D)
+        out[f"{name}_x"] = _bits(x)
+        out[f"{name}_out"] = _bits(tref.rms_rope_split_half(x, pe, scale, 1e-6))
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {len(out)} arrays")
 
 
 if __name__ == "__main__":

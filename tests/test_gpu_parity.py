@@ -781,3 +781,99 @@ def test_split_projection_rejects_bad_parts():
         int8.linear_split(x, w8, ws, parts=3)      # 48 columns: not a multiple of 32
     with pytest.raises(ValueError):
         int8.linear_split(x, w8, ws, parts=5)      # 144 rows do not split in 5
+
+
+# ------------------------------------------------------------------------ qkv consumer: RMS norm + rope
+
+def _pe(B, S, D, seed, fb=None):
+    g = torch.Generator().manual_seed(seed)
+    ang = torch.rand(B if fb is None else fb, S, 1, D // 2, generator=g) * 3.0
+    return torch.stack([torch.stack([ang.cos(), -ang.sin()], -1),
+                        torch.stack([ang.sin(), ang.cos()], -1)], -2)
+
+
+def _rope_close(got, ref, what):
+    """Same arithmetic, summed in a different order: a few outputs may move by a
+    bf16 ulp (the reference's own budget for that, triton/reference.py:45-53,
+    is 1e-3 relative)."""
+    ulps = np.abs(got.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32))
+    rel = rel_l2(got, ref)
+    print(f"\n{what}: {int((ulps > 0).sum())} of {got.size} differ, max {ulps.max()} ulp, "
+          f"rel-L2 {rel:.2e}")
+    assert (ulps > 0).mean() < 1e-2 and rel < 1e-3
+
+
+def test_rms_rope_dequant_matches_the_reference_fixture():
+    """The int32-accumulator consumer on the q and k slices of a fused qkv
+    accumulator (strided views, row stride 3*H*D) against the reference's torch
+    chain run on CPU (tests/golden/reference_rope.npz); the bf16 form on the
+    dequantized slices gives the same bits as the int32 form."""
+    from xpu_kernels import int8
+    import os
+    R = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_rope.npz"))
+    B, S, H, D = 1, 48, 3, 128
+    acc = torch.from_numpy(R["acc"]).to(DEV)
+    xs, ws = torch.from_numpy(R["xs"]).to(DEV), torch.from_numpy(R["ws"]).to(DEV)
+    scale, pe = torch.from_numpy(R["scale"]).to(DEV), torch.from_numpy(R["pe"]).to(DEV)
+    view = acc.view(B, S, 3 * H * D)
+    q_acc = view[:, :, :H * D].unflatten(-1, (H, D))
+    k_acc = view[:, :, H * D:2 * H * D].unflatten(-1, (H, D))
+    q, k = int8.rms_rope_split_half_dequant(q_acc, k_acc, pe, ws[:H * D], ws[H * D:2 * H * D],
+                                            xs.view(B, S), scale)
+    for name, got in (("q", q), ("k", k)):
+        _rope_close(bits(got), R[f"{name}_out"].reshape(B, S, H, D), f"rms_rope {name} vs reference")
+        xb = dev_bf16(R[f"{name}_x"].reshape(B, S, H, D))
+        assert torch.equal(int8.rms_rope(xb, pe, scale).view(torch.int16), got.view(torch.int16))
+
+
+@pytest.mark.parametrize("B,S,H,D,split,fb", [(2, 33, 5, 64, True, None), (1, 100, 2, 256, True, 1),
+                                             (3, 17, 4, 128, False, None), (2, 8, 1, 64, False, 1)])
+def test_rms_rope_matches_the_oracle(B, S, H, D, split, fb):
+    """Both rotations (split half, interleaved), D = 64 / 128 / 256, freqs per
+    batch or broadcast, several batches: the int32 form against the oracle,
+    and the bf16 form on the dequantized values equal to it."""
+    from xpu_kernels import int8
+    g = torch.Generator().manual_seed(B * 1000 + S + D)
+    acc = torch.randint(-(2 ** 22), 2 ** 22, (B, S, H, D), generator=g, dtype=torch.int32)
+    xs = torch.rand(B * S, generator=g) * 0.02 + 0.001
+    ws = torch.rand(H * D, generator=g) * 0.02 + 0.001
+    scale = torch.rand(D, generator=g) * 0.2 + 0.9
+    pe = _pe(B, S, D, D + S, fb)
+    got = int8.rms_rope_dequant(acc.to(DEV), pe.to(DEV), scale.to(DEV), xs.to(DEV), ws.to(DEV),
+                                1e-6, split)
+    ref = O.rms_rope(acc.numpy(), pe.numpy().reshape(pe.shape[0], S, D // 2, 2, 2), scale.numpy(),
+                     1e-6, split, xs.numpy(), ws.numpy())
+    _rope_close(bits(got), ref, f"rms_rope {B}x{S}x{H}x{D} split={split}")
+    x = torch.from_numpy(O.f32_to_bf16_bits(O.round_bf16(
+        (acc.numpy().astype(np.float32) * (ws.numpy().reshape(1, 1, H, D)
+                                           * xs.numpy().reshape(B, S, 1, 1)).astype(np.float32))
+        .astype(np.float32))).view(np.int16)).view(torch.bfloat16)
+    same = int8.rms_rope(x.to(DEV), pe.to(DEV), scale.to(DEV), 1e-6, split)
+    assert torch.equal(same.view(torch.int16), got.view(torch.int16))
+
+
+def test_split_projection_then_rms_rope_equals_the_accumulator_path():
+    """The fused pipeline (linear_split writes bf16 q, k, v; rms_rope reads them)
+    equals the reference's (linear_acc over cat(Wq, Wk, Wv), then the dequant
+    consumer on the int32 q and k slices), bit for bit."""
+    from xpu_kernels import int8
+    B, S, H, D, K = 2, 64, 4, 128, 1024
+    n = H * D
+    x = rand_bf16((B * S, K), 330, outliers=4).to(DEV)
+    w8s, wss = [], []
+    for i in range(3):
+        _, w8i, wsi = _prep(n, K, 331 + i)
+        w8s.append(torch.from_numpy(w8i).to(DEV))
+        wss.append(torch.from_numpy(wsi).to(DEV))
+    w8, ws = torch.cat(w8s), torch.cat(wss)
+    scale = (torch.rand(D, generator=torch.Generator().manual_seed(5)) * 0.2 + 0.9).to(DEV)
+    pe = _pe(B, S, D, 6).to(DEV)
+    q, k, v = int8.linear_split(x, w8, ws, None, parts=3)
+    fused = int8.rms_rope_split_half(q.view(B, S, H, D), k.view(B, S, H, D), pe, scale)
+    acc, xs = int8.linear_acc(x, w8, ws)
+    a3 = acc.view(B, S, 3 * n)
+    ref = int8.rms_rope_split_half_dequant(a3[:, :, :n].unflatten(-1, (H, D)),
+                                           a3[:, :, n:2 * n].unflatten(-1, (H, D)), pe,
+                                           ws[:n], ws[n:2 * n], xs.view(B, S), scale)
+    for a, b in zip(fused, ref):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))

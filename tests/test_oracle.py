@@ -206,3 +206,22 @@ def test_torch_cpu_restatement_of_convrot_linear_as_shipped(G):
     d = np.abs(O.bf16_bits_to_f32(got).astype(np.float64) - O.bf16_bits_to_f32(ref))
     assert (got != ref).mean() < 0.02 and d.max() <= 0.02 * np.abs(O.bf16_bits_to_f32(ref)).max()
     assert np.array_equal(T.hadamard_bf16().float().numpy(), O.hadamard_matrix().astype(np.float32))
+
+
+def test_rms_rope_restatement_matches_the_reference_chain():
+    """The oracle's RMS norm + rotary embedding (the consumer of the fused qkv
+    accumulator) against the reference's torch chain
+    (python/xpu_kernels/triton/reference.py:63-98) on the bf16 dequant of an
+    int32 accumulator slice, exactly as the reference's own probe builds its
+    expected value (tests/golden/reference_rope.npz); the int32 form with the
+    dequant folded in gives the same bits."""
+    import os
+    R = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_rope.npz"))
+    B, S, H, D = 1, 48, 3, 128
+    pe = R["pe"].reshape(B, S, D // 2, 2, 2)
+    for name, lo in (("q", 0), ("k", H * D)):
+        got = O.rms_rope(R[f"{name}_x"], pe, R["scale"], 1e-6, True)
+        assert np.array_equal(got, R[f"{name}_out"].reshape(got.shape))
+        acc = R["acc"][:, lo:lo + H * D].reshape(B, S, H, D)
+        got_acc = O.rms_rope(acc, pe, R["scale"], 1e-6, True, R["xs"], R["ws"][lo:lo + H * D])
+        assert np.array_equal(got_acc, got)
