@@ -656,9 +656,12 @@ int xpuint8_rms_rope_stream(const void *stream, const void *x, int32_t x_is_int3
         set_error("a required pointer is null");
         return 2;
     }
-    if (!aligned16(freqs) || (reinterpret_cast<uintptr_t>(x) & (x_is_int32 ? 3u : 1u)) ||
-        (reinterpret_cast<uintptr_t>(out) & 1u)) {
-        set_error("rms_rope: freqs must be 16-byte aligned, x and out aligned to their element size");
+    // 16-byte (int32) or 8-byte (bf16) accesses of four elements per head run
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+    if (!aligned16(freqs) || !aligned16(weight) || (x_is_int32 && (!aligned16(w_scale) || (xa & 15u) || (ldx % 4))) ||
+        (!x_is_int32 && ((xa & 7u) || (ldx % 4))) || (reinterpret_cast<uintptr_t>(out) & 7u) || (ldo % 4)) {
+        set_error("rms_rope: freqs, weight (and w_scale) need 16-byte aligned bases; x (16 bytes "
+                  "for int32, 8 for bf16) and out (8 bytes) aligned, row strides multiples of 4");
         return 2;
     }
     return launch_rms_rope(as_stream(stream), x, x_is_int32 != 0, ldx, x_scale, w_scale, weight, freqs,

@@ -664,6 +664,10 @@ def _rope_freqs(freqs_cis, B, S, D, dev):
     return f.to(device=dev, dtype=torch.float32).contiguous()
 
 
+def _aligned16(t):
+    return t.clone() if t.data_ptr() % 16 else t
+
+
 def _rms_rope(x, freqs_cis, scale, epsilon, split_half, x_scale=None, w_scale=None):
     lib = _lib()
     is_acc = x_scale is not None
@@ -672,18 +676,25 @@ def _rms_rope(x, freqs_cis, scale, epsilon, split_half, x_scale=None, w_scale=No
     if not is_acc and x.dtype != torch.bfloat16:
         raise TypeError("x must be bfloat16")
     ld, B, S, H, D = _rope_rows(x, "x")
+    # the kernel reads runs of four elements: 16-byte (int32) / 8-byte (bf16)
+    # aligned rows; an odd view is copied first
+    if x.data_ptr() % (16 if is_acc else 8) or ld % 4:
+        x = x.contiguous() if not x.is_contiguous() else x.clone()
+        ld = H * D
     dev = x.device
-    f = _rope_freqs(freqs_cis, B, S, D, dev)
-    w = scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+    f = _aligned16(_rope_freqs(freqs_cis, B, S, D, dev))
+    w = _aligned16(scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous())
     if w.numel() != D:
         raise ValueError(f"scale must have {D} elements")
     xs = ws = None
     if is_acc:
         xs = x_scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
-        ws = w_scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+        ws = _aligned16(w_scale.reshape(-1).to(device=dev, dtype=torch.float32).contiguous())
         if xs.numel() != B * S or ws.numel() != H * D:
             raise ValueError("x_scale must have B*S elements and w_scale H*D")
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dev)
+    if out.numel() == 0:
+        return out
     rc = lib.xpuint8_rms_rope_stream(_stream(dev), ctypes.c_void_p(x.data_ptr()), 1 if is_acc else 0,
                                      ld, _ptr(xs), _ptr(ws), _ptr(w), _ptr(f), f.shape[0], f.shape[1],
                                      _ptr(out), H * D, B, S, H, D, float(epsilon),

@@ -514,9 +514,11 @@ def test_colquant_is_bit_exact(m, n):
     assert np.array_equal(bits(gq), qr)
 
 
-def test_linear_dx_int8_matches_the_oracle():
+@pytest.mark.parametrize("m,n,k", [(256, 512, 1280), (100, 208, 768), (333, 1040, 256)])
+def test_linear_dx_int8_matches_the_oracle(m, n, k):
+    """The one-call entry (row quantizer, GEMM with MN-major B, rotate), with
+    ragged M and N."""
     from xpu_kernels import int8
-    m, n, k = 256, 512, 1280
     _, w8, ws = _prep(n, k, 150)
     dy = rand_bf16((m, n), 151, scale=1e-3)
     got = bits(int8.linear_dx_int8(dy.to(DEV), torch.from_numpy(w8).to(DEV),
@@ -524,9 +526,11 @@ def test_linear_dx_int8_matches_the_oracle():
     assert np.array_equal(got, O.linear_dx_int8(bits(dy), w8, ws))
 
 
-def test_linear_dw_int8_matches_the_oracle():
+@pytest.mark.parametrize("m,n,k", [(512, 256, 1280), (272, 208, 512), (100, 256, 768)])
+def test_linear_dw_int8_matches_the_oracle(m, n, k):
+    """The one-call entry (column quantizer, GEMM with both operands MN-major,
+    rotate), with ragged M and N."""
     from xpu_kernels import int8
-    m, n, k = 512, 256, 1280
     x = rand_bf16((m, k), 160)
     dy = rand_bf16((m, n), 161, scale=1e-3)
     xq, xs = int8.quantize(x.to(DEV))
@@ -827,7 +831,8 @@ def test_rms_rope_dequant_matches_the_reference_fixture():
 
 
 @pytest.mark.parametrize("B,S,H,D,split,fb", [(2, 33, 5, 64, True, None), (1, 100, 2, 256, True, 1),
-                                             (3, 17, 4, 128, False, None), (2, 8, 1, 64, False, 1)])
+                                             (3, 17, 4, 128, False, None), (2, 8, 1, 64, False, 1),
+                                             (4, 512, 40, 128, True, None)])
 def test_rms_rope_matches_the_oracle(B, S, H, D, split, fb):
     """Both rotations (split half, interleaved), D = 64 / 128 / 256, freqs per
     batch or broadcast, several batches: the int32 form against the oracle,
@@ -850,6 +855,16 @@ def test_rms_rope_matches_the_oracle(B, S, H, D, split, fb):
         .astype(np.float32))).view(np.int16)).view(torch.bfloat16)
     same = int8.rms_rope(x.to(DEV), pe.to(DEV), scale.to(DEV), 1e-6, split)
     assert torch.equal(same.view(torch.int16), got.view(torch.int16))
+
+
+def test_rms_rope_empty_rows():
+    """No rows: an empty [B, 0, H, D] result and no launch (the reference's
+    wrappers launch a (S, B) grid, empty here: triton/rope.py:360-376)."""
+    from xpu_kernels import int8
+    pe = _pe(1, 1, 128, 0).to(DEV)
+    out = int8.rms_rope(torch.empty(1, 0, 4, 128, dtype=torch.bfloat16, device=DEV), pe[:, :0],
+                        torch.ones(128, device=DEV))
+    assert out.shape == (1, 0, 4, 128)
 
 
 def test_split_projection_then_rms_rope_equals_the_accumulator_path():
