@@ -91,6 +91,8 @@ def main(argv=None):
     ap.add_argument("--K", type=int, default=1280)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--sets", type=int, default=2)
+    ap.add_argument("--act", type=int, default=4,
+                    help="dequant_act / ffn: 3 situ, 4 GEGLU (paired), 5 GELU-erf (unpaired)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib()
@@ -199,20 +201,21 @@ def main(argv=None):
         t = _time(fn, a.iters, st)
         res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9}
     elif a.case == "dequant_act":
-        ACC = [torch.randint(-2 ** 20, 2 ** 20, (M, 2 * K), generator=g, device=dev,
+        halves = 1 if a.act == 5 else 2
+        ACC = [torch.randint(-2 ** 20, 2 ** 20, (M, halves * K), generator=g, device=dev,
                              dtype=torch.int32) for _ in range(S)]
         Q = [torch.empty(M, K, dtype=torch.int8, device=dev) for _ in range(S)]
         sc = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(S)]
-        xs, ws = f32(M), f32(2 * K)
+        xs, ws = f32(M), f32(halves * K)
 
         def fn(i):
             j = i % S
             rc = lib.xpuint8_dequant_act_quantize_stream(_stream(dev), _ptr(ACC[j]), _ptr(Q[j]), _ptr(sc[j]),
-                                                         _ptr(xs), _ptr(ws), M, K, 4)
+                                                         _ptr(xs), _ptr(ws), M, K, a.act)
             assert rc == 0, lib.xpuint8_last_error()
-        nbytes = 8 * M * K + 8 * K + M * K + 8 * M
+        nbytes = halves * (4 * M * K + 4 * K) + M * K + 8 * M
         t = _time(fn, a.iters, st)
-        res = {"case": a.case, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9}
+        res = {"case": a.case, "act": a.act, "ms": t, "GBps": nbytes / (t * 1e-3) / 1e9}
     elif a.case == "linear":
         X = [bf(M, K) for _ in range(S)]
         w8, ws = ops.prepare_weight(bf(N, K, s=0.02))
@@ -222,16 +225,19 @@ def main(argv=None):
         t = _time(fn, a.iters, st)
         res = {"case": a.case, "ms": t, "TOPS": 2.0 * M * N * K / (t * 1e-3) / 1e12}
     elif a.case == "ffn":
+        # N: the up-projection's rows for a paired activation ([hidden | gate])
         inner = N // 2
+        act = {3: "situ", 4: "geglu_erf", 5: "gelu_erf"}[a.act]
+        n_up = inner if act == "gelu_erf" else N
         X = [bf(M, K) for _ in range(S)]
-        up8, ups = ops.prepare_weight(bf(N, K, s=0.02))
+        up8, ups = ops.prepare_weight(bf(n_up, K, s=0.02))
         dn8, dns = ops.prepare_weight(bf(K, inner, s=0.02))
 
         def fn(i):
-            ops.ffn(X[i % S], up8, ups, dn8, dns, act="geglu_erf")
+            ops.ffn(X[i % S], up8, ups, dn8, dns, act=act)
         t = _time(fn, a.iters, st)
-        res = {"case": a.case, "ms": t,
-               "TOPS": (2.0 * M * N * K + 2.0 * M * inner * K) / (t * 1e-3) / 1e12}
+        res = {"case": a.case, "act": act, "ms": t,
+               "TOPS": (2.0 * M * n_up * K + 2.0 * M * inner * K) / (t * 1e-3) / 1e12}
     elif a.case in ("dx", "dw"):
         x = bf(M, K)
         w8, ws = ops.prepare_weight(bf(N, K, s=0.02))

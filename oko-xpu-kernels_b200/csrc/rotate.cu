@@ -27,6 +27,7 @@
 // row abs-max through shared memory, and only then are quantized.  Output
 // bytes are staged back through the slot's tile so every global store is a
 // contiguous 16-byte store.
+#include "act.cuh"
 #include "common.cuh"
 #include "internal.h"
 
@@ -35,43 +36,6 @@ namespace {
 
 constexpr int kTileFloats = 272;  // 16x16 floats + 16 floats of skew between slots
 
-__device__ __forceinline__ float gelu_erf_f(float x) {
-    const float t = __fmul_rn(x, 0.7071067811865476f);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(t)));
-}
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float x2 = __fmul_rn(x, x);
-    const float inner = __fmul_rn(__fmul_rn(0.7978845608028654f, x),
-                                  __fadd_rn(1.0f, __fmul_rn(0.044715f, x2)));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-// MossImage's situ with the reference's bf16 rounding points (src/xpuint8.cpp:142-160)
-__device__ __forceinline__ float situ_f(float h, float g) {
-    const float tg = round_bf16(tanhf(round_bf16(__fdiv_rn(g, 4.0f))));
-    const float sg = round_bf16(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
-    const float th = round_bf16(tanhf(round_bf16(__fdiv_rn(h, 25.0f))));
-    const float p = round_bf16(__fmul_rn(tg, sg));
-    return round_bf16(__fmul_rn(p, th));
-}
-// the fused input activation (src/xpuint8.cpp:190-220); a, b are exact bf16
-template <int ACT>
-__device__ __forceinline__ float activate(float a, float b) {
-    if constexpr (ACT == 0) {
-        return a;
-    } else if constexpr (ACT == 1) {
-        return round_bf16(gelu_tanh_f(a));
-    } else if constexpr (ACT == 2) {  // swiglu: a = gate, b = up
-        const float silu = round_bf16(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
-        return round_bf16(__fmul_rn(silu, b));
-    } else if constexpr (ACT == 3) {  // situ: a = hidden, b = gate
-        return situ_f(a, b);
-    } else if constexpr (ACT == 4) {  // geglu: a = hidden, b = gate
-        return round_bf16(__fmul_rn(a, round_bf16(gelu_erf_f(b))));
-    } else {
-        return round_bf16(gelu_erf_f(a));
-    }
-}
-__host__ __device__ constexpr bool act_paired(int act) { return act == 2 || act == 3 || act == 4; }
 
 struct RotParams {
     const void *in;

@@ -36,6 +36,7 @@
 #include <cstdlib>
 #include <string>
 
+#include "act.cuh"
 #include "common.cuh"
 #include "internal.h"
 
@@ -59,41 +60,6 @@ struct BulkParams {
     uint32_t out_stage_bytes;
 };
 
-__device__ __forceinline__ float gelu_erf_f(float x) {
-    const float t = __fmul_rn(x, 0.7071067811865476f);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(t)));
-}
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float x2 = __fmul_rn(x, x);
-    const float inner = __fmul_rn(__fmul_rn(0.7978845608028654f, x),
-                                  __fadd_rn(1.0f, __fmul_rn(0.044715f, x2)));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-__device__ __forceinline__ float situ_f(float h, float g) {
-    const float tg = round_bf16(tanhf(round_bf16(__fdiv_rn(g, 4.0f))));
-    const float sg = round_bf16(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
-    const float th = round_bf16(tanhf(round_bf16(__fdiv_rn(h, 25.0f))));
-    const float p = round_bf16(__fmul_rn(tg, sg));
-    return round_bf16(__fmul_rn(p, th));
-}
-template <int ACT>
-__device__ __forceinline__ float activate(float a, float b) {
-    if constexpr (ACT == 0) {
-        return a;
-    } else if constexpr (ACT == 1) {
-        return round_bf16(gelu_tanh_f(a));
-    } else if constexpr (ACT == 2) {
-        const float silu = round_bf16(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))));
-        return round_bf16(__fmul_rn(silu, b));
-    } else if constexpr (ACT == 3) {
-        return situ_f(a, b);
-    } else if constexpr (ACT == 4) {
-        return round_bf16(__fmul_rn(a, round_bf16(gelu_erf_f(b))));
-    } else {
-        return round_bf16(gelu_erf_f(a));
-    }
-}
-__host__ __device__ constexpr bool act_paired(int act) { return act == 2 || act == 3 || act == 4; }
 
 // the 16 values lane l owns of one group, loaded from global memory (row = absolute row)
 template <int MODE, int ACT>
@@ -929,11 +895,6 @@ int launch_rotate_bulk(cudaStream_t s, int mode, int act, const void *in, const 
             const int64_t r = std::min<int64_t>(32, (2 * c) / G);
             const double fill = static_cast<double>(r * G) / (2 * c);
             if (fill > best_fill + 1e-9) { best_fill = fill; slots = c; }
-        }
-        // XPUINT8_ROTATE_SLOTS=8|10|12|16 fixes the team size (tuning)
-        if (const char *f = std::getenv("XPUINT8_ROTATE_SLOTS")) {
-            const int v = std::atoi(f);
-            if ((v == 8 || v == 10 || v == 12 || v == 16) && G <= 2 * v) slots = v;
         }
         p.R = static_cast<int>(std::min<int64_t>(32, (2 * slots) / G));
         const int64_t nbd = (M + p.R - 1) / p.R;
