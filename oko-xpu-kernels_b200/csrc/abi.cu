@@ -519,13 +519,14 @@ DxLayout dx_layout(int64_t M, int64_t N, int64_t K) {
     return L;
 }
 struct DwLayout {
-    size_t gq, tg, dwr, total;
+    size_t gq, tg, amax, dwr, total;
 };
 DwLayout dw_layout(int64_t M, int64_t N, int64_t K) {
     DwLayout L{};
     size_t off = 0;
     L.gq = off; off += align256(static_cast<size_t>(M) * N);       // column-quantized dy * xs
     L.tg = off; off += align256(static_cast<size_t>(N) * 4);       // its column scales
+    L.amax = off; off += align256(static_cast<size_t>(N) * 4);     // its column maxima
     L.dwr = off; off += align256(static_cast<size_t>(N) * K * 2);  // dW before the rotation
     L.total = off;
     return L;
@@ -596,7 +597,9 @@ int xpuint8_linear_dw_int8_stream(const void *stream, const void *dy, const int8
     float *tg = reinterpret_cast<float *>(ws + L.tg);
     void *dwr = ws + L.dwr;
     // g = dy * xs[m] quantized per column n (over the tokens m)
-    if (int rc = launch_colquant(s, dy, x_scale, gq, tg, M, N)) return rc;
+    if (int rc = launch_colquant(s, dy, x_scale, gq, tg, M, N,
+                                 reinterpret_cast<unsigned int *>(ws + L.amax)))
+        return rc;
     // dwr [N, K] = bf16(float(gq^T @ xq) * tg[n]): both operands MN-major
     if (int rc = int_mm_common(s, kEpiDequantBf16, gq, xq, dwr, tg, nullptr, nullptr, N, K, M, 2, K,
                                true))

@@ -36,8 +36,10 @@ int launch_dequant_epilogue(cudaStream_t s, const int32_t *acc, void *out, const
 // row / column quantizers (rowquant.cu)
 int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, int8_t *q,
                         float *scale, int64_t M, int64_t K);
+// amax_ws: N words of scratch for the column maxima (the scales are then
+// made inside the quantizing pass); NULL: tg holds them (one launch more)
 int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t *gq, float *tg,
-                    int64_t M, int64_t N);
+                    int64_t M, int64_t N, unsigned int *amax_ws = nullptr);
 
 // tcgen05 int8 GEMM (gemm_i8.cu)
 // kEpiDequantWide: the dequant epilogue storing 32 rows x 64 columns (128-byte

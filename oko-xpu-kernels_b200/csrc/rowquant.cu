@@ -190,54 +190,74 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
     }
 }
 
-// Column quantizer tiles: a 256-thread CTA covers kColRows rows x 256
-// columns; thread (ty, tx) = (threadIdx.x / 32, threadIdx.x % 32) owns the 8
-// columns 8 tx .. 8 tx + 7 of the tile and the rows ty, ty + 8, ... of it, so
-// a warp reads 512 contiguous bytes of a row and keeps four loads in flight.
-constexpr int kColRows = 128;
+// Column quantizer tiles: a 256-thread CTA covers a run of rows x 512
+// columns; lane l of warp w owns the 16 columns 16 l .. 16 l + 15 of the
+// tile (32 bytes of a row: a warp reads 1 KB contiguous) and the rows
+// w, w + 8, ... of the run, keeping four rows of loads in flight.
+constexpr int kColW = 512;     // columns per tile
+constexpr int kColLanes = 8;   // rows read at once (one per warp)
 
-// column abs-max of g = dy * xs: a CTA reduces its tile over rows in shared
-// memory and posts one atomicMax per column (on the bit pattern of a
-// non-negative float).  dy is read with the normal L2 policy: the second pass
-// (colquant_kernel) reads it again, from L2 when it fits (the C4 gradient,
-// 42 MB, does), and streams it out of the cache there.
+// the 16 fp32 values g = dy * x of a lane's 16 columns of one row, as 8 pairs
+__device__ __forceinline__ void load_g16(const uint16_t *p, float x, f2 (&g)[8]) {
+    const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p));
+    const uint4 b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
+    const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const f2 x2 = mk2(x, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = mul2(mk2(bf16_lo(u[j]), bf16_hi(u[j])), x2);
+}
+
+// Pass 1: column abs-maxima of g = dy * xs over a run of rows, reduced over
+// the CTA's row lanes in shared memory and posted with one atomicMax per
+// column on the bit pattern of a non-negative float into amax (zeroed
+// before).  dy is read with the normal L2 policy, so that the second pass
+// finds it in L2 when it fits (config C4's 42 MB does).
 __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict__ dy,
                                                       const float *__restrict__ xs,
-                                                      unsigned int *__restrict__ amax,
-                                                      int64_t M, int64_t N) {
-    __shared__ float red[8][256];
+                                                      unsigned int *__restrict__ amax, int64_t M,
+                                                      int64_t N, int64_t rows) {
+    __shared__ float red[kColLanes][kColW];
     pdl_wait();
     pdl_trigger();
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + 8 * tx;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kColRows;
-    const int64_t m1 = min(M, m0 + kColRows);
-    float mx[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (n < N) {
-#pragma unroll 8
-        for (int64_t m = m0 + ty; m < m1; m += 8) {
-            const float x = __ldg(xs + m);
-            const uint4 w = __ldcg(reinterpret_cast<const uint4 *>(dy + m * N + n));
-            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * kColW + 16 * l;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * rows;
+    const int64_t m1 = min(M, m0 + rows);
+    float mx[16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                mx[2 * j] = fmaxf(mx[2 * j], fabsf(__fmul_rn(bf16_lo(u[j]), x)));
-                mx[2 * j + 1] = fmaxf(mx[2 * j + 1], fabsf(__fmul_rn(bf16_hi(u[j]), x)));
+    for (int t = 0; t < 16; ++t) mx[t] = 0.f;
+    if (n < N) {
+#pragma unroll 4
+        for (int64_t m = m0 + w; m < m1; m += kColLanes) {
+            f2 g[8];
+            load_g16(dy + m * N + n, __ldg(xs + m), g);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float a, b;
+                un2(g[j], a, b);
+                mx[2 * j] = fmaxf(mx[2 * j], fabsf(a));
+                mx[2 * j + 1] = fmaxf(mx[2 * j + 1], fabsf(b));
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) red[ty][8 * tx + t] = mx[t];
+    for (int t = 0; t < 16; t += 4)
+        *reinterpret_cast<float4 *>(&red[w][16 * l + t]) = make_float4(mx[t], mx[t + 1], mx[t + 2], mx[t + 3]);
     __syncthreads();
-    const int64_t c = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-    if (c < N) {
-        float v = red[0][threadIdx.x];
 #pragma unroll
-        for (int r = 1; r < 8; ++r) v = fmaxf(v, red[r][threadIdx.x]);
-        atomicMax(amax + c, __float_as_uint(v));
+    for (int h = 0; h < kColW / 256; ++h) {
+        const int c = threadIdx.x + 256 * h;
+        const int64_t col = static_cast<int64_t>(blockIdx.x) * kColW + c;
+        if (col < N) {
+            float v = red[0][c];
+#pragma unroll
+            for (int r = 1; r < kColLanes; ++r) v = fmaxf(v, red[r][c]);
+            atomicMax(amax + col, __float_as_uint(v));
+        }
     }
 }
 
+// tg[n] = max(amax[n] / 127, 1e-30) in place (after the atomic form of pass 1)
 __global__ void colscale_kernel(float *tg, int64_t N) {
     pdl_wait();
     pdl_trigger();
@@ -249,44 +269,75 @@ __global__ void colscale_kernel(float *tg, int64_t N) {
     }
 }
 
-// gq = clamp(rint(g / tg[n]), +-127), g = dy * xs; each thread's 8 column
-// reciprocals are computed once
+// Pass 2: gq = clamp(rint(g / tg[n]), +-127) over a run of rows, 16 codes
+// per lane and row in one 16-byte store.  FROM_AMAX: the CTA makes the scales
+// of its 512 columns from the column maxima of pass 1 (amax; the CTAs of the
+// first run also write them to tg); otherwise it reads them from tg.  Each
+// column's reciprocal is made once per CTA.
+template <bool FROM_AMAX>
 __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restrict__ dy,
                                                        const float *__restrict__ xs,
-                                                       const float *__restrict__ tg,
-                                                       int8_t *__restrict__ gq, int64_t M,
-                                                       int64_t N) {
+                                                       const unsigned int *__restrict__ amax,
+                                                       float *__restrict__ tg, int8_t *__restrict__ gq,
+                                                       int64_t M, int64_t N, int64_t rows) {
+    __shared__ float s_t[kColW], s_y[kColW];
     pdl_wait();
     pdl_trigger();
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + 8 * tx;
-    if (n >= N) return;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kColRows;
-    const int64_t m1 = min(M, m0 + kColRows);
-    float t[8], y[8];
-    {
-        const float4 t0 = __ldg(reinterpret_cast<const float4 *>(tg + n));
-        const float4 t1 = __ldg(reinterpret_cast<const float4 *>(tg + n) + 1);
-        t[0] = t0.x; t[1] = t0.y; t[2] = t0.z; t[3] = t0.w;
-        t[4] = t1.x; t[5] = t1.y; t[6] = t1.z; t[7] = t1.w;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = rcp_rn(t[j]);
-    }
-#pragma unroll 4
-    for (int64_t m = m0 + ty; m < m1; m += 8) {
-        const float x = __ldg(xs + m);
-        const uint4 w = __ldcs(reinterpret_cast<const uint4 *>(dy + m * N + n));
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-        uint32_t b[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            b[2 * j] = q_div(__fmul_rn(bf16_lo(u[j]), x), t[2 * j], y[2 * j]);
-            b[2 * j + 1] = q_div(__fmul_rn(bf16_hi(u[j]), x), t[2 * j + 1], y[2 * j + 1]);
+    for (int h = 0; h < kColW / 256; ++h) {
+        const int c = threadIdx.x + 256 * h;
+        const int64_t col = static_cast<int64_t>(blockIdx.x) * kColW + c;
+        float t = 1.f, y = 1.f;
+        if (col < N) {
+            if constexpr (FROM_AMAX) {
+                row_scale_inv(__uint_as_float(amax[col]), t);  // t as colscale_kernel makes it
+                if (blockIdx.y == 0) tg[col] = t;
+            } else {
+                t = tg[col];
+            }
+            y = rcp_rn(t);
         }
-        uint2 o;
+        s_t[c] = t;
+        s_y[c] = y;
+    }
+    __syncthreads();
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * kColW + 16 * l;
+    if (n >= N) return;
+    f2 t2[8], y2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        t2[j] = mk2(s_t[16 * l + 2 * j], s_t[16 * l + 2 * j + 1]);
+        y2[j] = mk2(s_y[16 * l + 2 * j], s_y[16 * l + 2 * j + 1]);
+    }
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * rows;
+    const int64_t m1 = min(M, m0 + rows);
+    const f2 one = mk2(1.0f, 1.0f), magic = mk2(12582912.0f, 12582912.0f);
+#pragma unroll 4
+    for (int64_t m = m0 + w; m < m1; m += kColLanes) {
+        f2 g[8];
+        load_g16(dy + m * N + n, __ldg(xs + m), g);
+        uint32_t b[16];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            // RN(g / t) by Markstein's correction of RN(g * y), then
+            // RN(q + 1.5 * 2^23), whose low byte is the code (the sum as an
+            // FMA with a unit product: a packed multiply feeding a packed add
+            // would be contracted into one rounding)
+            const f2 q0 = mul2(g[j], y2[j]);
+            const f2 r = fma2(f2{q0.v ^ 0x8000000080000000ull}, t2[j], g[j]);  // -q0 * t + g
+            const f2 q = fma2(fma2(r, y2[j], q0), one, magic);
+            float c0, c1;
+            un2(q, c0, c1);
+            b[2 * j] = __float_as_uint(c0) & 0xFFu;
+            b[2 * j + 1] = __float_as_uint(c1) & 0xFFu;
+        }
+        uint4 o;
         o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
         o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
-        __stcs(reinterpret_cast<uint2 *>(gq + m * N + n), o);
+        o.z = b[8] | (b[9] << 8) | (b[10] << 16) | (b[11] << 24);
+        o.w = b[12] | (b[13] << 8) | (b[14] << 16) | (b[15] << 24);
+        __stcs(reinterpret_cast<uint4 *>(gq + m * N + n), o);
     }
 }
 
@@ -364,17 +415,30 @@ int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, i
 }
 
 int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t *gq, float *tg,
-                    int64_t M, int64_t N) {
+                    int64_t M, int64_t N, unsigned int *amax_ws) {
     const uint16_t *d = static_cast<const uint16_t *>(dy);
-    if ((M + kColRows - 1) / kColRows > 65535) {
-        set_error("M is too large for the column quantizer");
+    const int64_t blocks = (N + kColW - 1) / kColW;
+    // runs of rows (a multiple of the row lanes) so that each pass is about
+    // one wave of resident CTAs
+    auto split = [&](int per, int64_t &runs, int64_t &rows) {
+        const int64_t want = std::max<int64_t>(1, static_cast<int64_t>(num_sms()) * per / blocks);
+        rows = (M + want - 1) / want;
+        rows = (rows + kColLanes - 1) / kColLanes * kColLanes;
+        runs = (M + rows - 1) / rows;
+    };
+    int64_t runs_a, rows_a, runs_q, rows_q;
+    split(resident_per_sm(colamax_kernel, 256), runs_a, rows_a);
+    split(amax_ws ? resident_per_sm(colquant_kernel<true>, 256) : resident_per_sm(colquant_kernel<false>, 256),
+          runs_q, rows_q);
+    if (runs_a > 65535 || runs_q > 65535 || blocks > 0x7FFFFFFF) {
+        set_error("the gradient is too large for the column quantizer");
         return 2;
     }
-    if (cudaMemsetAsync(tg, 0, static_cast<size_t>(N) * sizeof(float), s) != cudaSuccess)
+    unsigned int *amax = amax_ws ? amax_ws : reinterpret_cast<unsigned int *>(tg);
+    if (cudaMemsetAsync(amax, 0, static_cast<size_t>(N) * sizeof(float), s) != cudaSuccess)
         return launch_status("colquant memset");
-    const dim3 grid(static_cast<unsigned>((N + 255) / 256), static_cast<unsigned>((M + kColRows - 1) / kColRows));
-    // the three kernels launch with programmatic serialization (each waits
-    // for the one before it before touching memory)
+    // the kernels launch with programmatic serialization (each waits for the
+    // one before it before touching memory)
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -383,17 +447,20 @@ int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cfg.blockDim = dim3(256);
-    cfg.gridDim = grid;
-    unsigned int *amax = reinterpret_cast<unsigned int *>(tg);
-    if (cudaLaunchKernelEx(&cfg, colamax_kernel, d, x_scale, amax, M, N) != cudaSuccess)
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(runs_a));
+    if (cudaLaunchKernelEx(&cfg, colamax_kernel, d, x_scale, amax, M, N, rows_a) != cudaSuccess)
         return launch_status("colquant (column maxima)");
-    cfg.gridDim = dim3(static_cast<unsigned>((N + 255) / 256));
-    if (cudaLaunchKernelEx(&cfg, colscale_kernel, tg, N) != cudaSuccess)
-        return launch_status("colquant (scales)");
-    cfg.gridDim = grid;
-    if (cudaLaunchKernelEx(&cfg, colquant_kernel, d, x_scale, static_cast<const float *>(tg), gq, M, N) !=
-        cudaSuccess)
-        return launch_status("colquant");
+    if (!amax_ws) {
+        cfg.gridDim = dim3(static_cast<unsigned>((N + 255) / 256));
+        if (cudaLaunchKernelEx(&cfg, colscale_kernel, tg, N) != cudaSuccess)
+            return launch_status("colquant (scales)");
+    }
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(runs_q));
+    const unsigned int *ca = amax;
+    const cudaError_t e = amax_ws
+        ? cudaLaunchKernelEx(&cfg, colquant_kernel<true>, d, x_scale, ca, tg, gq, M, N, rows_q)
+        : cudaLaunchKernelEx(&cfg, colquant_kernel<false>, d, x_scale, ca, tg, gq, M, N, rows_q);
+    if (e != cudaSuccess) return launch_status("colquant");
     return launch_status("colquant");
 }
 
