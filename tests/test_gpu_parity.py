@@ -514,7 +514,7 @@ def test_colquant_is_bit_exact(m, n):
     assert np.array_equal(bits(gq), qr)
 
 
-@pytest.mark.parametrize("m,n,k", [(256, 512, 1280), (100, 208, 768), (333, 1040, 256)])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 1280), (100, 208, 768), (333, 1040, 256), (4000, 640, 1280)])
 def test_linear_dx_int8_matches_the_oracle(m, n, k):
     """The one-call entry (row quantizer, GEMM with MN-major B, rotate), with
     ragged M and N."""
@@ -526,7 +526,7 @@ def test_linear_dx_int8_matches_the_oracle(m, n, k):
     assert np.array_equal(got, O.linear_dx_int8(bits(dy), w8, ws))
 
 
-@pytest.mark.parametrize("m,n,k", [(512, 256, 1280), (272, 208, 512), (100, 256, 768)])
+@pytest.mark.parametrize("m,n,k", [(512, 256, 1280), (272, 208, 512), (100, 256, 768), (384, 3872, 1280)])
 def test_linear_dw_int8_matches_the_oracle(m, n, k):
     """The one-call entry (column quantizer, GEMM with both operands MN-major,
     rotate), with ragged M and N."""
