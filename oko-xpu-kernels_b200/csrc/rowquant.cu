@@ -40,6 +40,16 @@ __device__ __forceinline__ uint32_t q_div(float x, float s, float y) {
     return __float_as_uint(__fadd_rn(div_by_rcp(x, s, y), 12582912.0f)) & 0xFFu;
 }
 
+// q_div on a pair of values, as packed fp32x2 operations (each lane of a
+// packed operation rounds as the scalar one): the two codes in the low bytes
+// of the halves.  The final add is an FMA with a unit product, because ptxas
+// contracts a packed multiply feeding a packed add into one rounding.
+__device__ __forceinline__ f2 q_div2(f2 x, f2 s, f2 y) {
+    const f2 q0 = mul2(x, y);
+    const f2 r = fma2(f2{q0.v ^ 0x8000000080000000ull}, s, x);  // x - s q0, exact
+    return fma2(fma2(r, y, q0), mk2(1.0f, 1.0f), mk2(12582912.0f, 12582912.0f));
+}
+
 template <bool COLSCALE>
 __device__ __forceinline__ void load8(const uint16_t *x, const float *cs, int64_t k, float (&v)[8]) {
     const uint4 w = *reinterpret_cast<const uint4 *>(x + k);
@@ -153,10 +163,14 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
             }
         }
         if constexpr (COLSCALE) {
+            // bf16(x * bf16(col_scale)): a packed product and one conversion per pair
 #pragma unroll
             for (int i = 0; i < CH * 4; ++i) {
-                v[2 * i] = round_bf16(__fmul_rn(v[2 * i], bf16_lo(csb[i])));
-                v[2 * i + 1] = round_bf16(__fmul_rn(v[2 * i + 1], bf16_hi(csb[i])));
+                float a, b;
+                un2(mul2(mk2(v[2 * i], v[2 * i + 1]), mk2(bf16_lo(csb[i]), bf16_hi(csb[i]))), a, b);
+                round_bf16x2(a, b);
+                v[2 * i] = a;
+                v[2 * i + 1] = b;
             }
         }
         load(row + gridDim.x, raw);  // the next row's loads fly meanwhile
@@ -172,14 +186,18 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
         const float y = row_scale_inv(rm, s);
         if (t == 0) scale[row] = s;
         int8_t *qr = q + row * K;
+        const f2 s2 = mk2(s, s), y2 = mk2(y, y);
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             const int ch = t + 128 * c;
             if (ch < nch) {
                 uint32_t b[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    b[j] = q_div(v[8 * c + j], s, y);
+                for (int j = 0; j < 8; j += 2) {
+                    float c0, c1;
+                    un2(q_div2(mk2(v[8 * c + j], v[8 * c + j + 1]), s2, y2), c0, c1);
+                    b[j] = __float_as_uint(c0) & 0xFFu;
+                    b[j + 1] = __float_as_uint(c1) & 0xFFu;
                 }
                 uint2 o;
                 o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
