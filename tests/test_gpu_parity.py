@@ -177,6 +177,27 @@ def test_quantize_full_c5_every_code():
         assert np.array_equal(bits(q[r:r + 8192]), qr), r
 
 
+def test_geglu_halves_are_not_swapped():
+    """The reference's half-order probe (debug/verify_ffn_geglu.py:116-127):
+    hidden = 1, gate = -2 through the fused quantizer equals the torch chain
+    quantize(hidden * gelu(gate)) bit for bit (the swapped halves would give
+    -2 * gelu(1)); the same for the dequant + activation path, whose int32
+    accumulators dequantize to those values."""
+    from xpu_kernels import int8
+    m, k = 8, 256
+    x = torch.zeros(m, 2 * k, dtype=torch.bfloat16, device=DEV)
+    x[:, :k], x[:, k:] = 1.0, -2.0
+    hidden, gate = x.chunk(2, dim=-1)
+    q_ref, s_ref = int8.quantize((hidden * torch.nn.functional.gelu(gate)).contiguous())
+    q, s = int8.quantize_act(x, "geglu_erf")
+    assert torch.equal(q, q_ref) and torch.equal(s.view(torch.int32), s_ref.view(torch.int32))
+    acc = torch.zeros(m, 2 * k, dtype=torch.int32, device=DEV)
+    acc[:, :k], acc[:, k:] = 1, -2
+    ones = torch.ones(m, dtype=torch.float32, device=DEV)
+    q2, s2 = int8.dequant_act_quantize(acc, ones, torch.ones(2 * k, dtype=torch.float32, device=DEV), "geglu_erf")
+    assert torch.equal(q2, q_ref) and torch.equal(s2.view(torch.int32), s_ref.view(torch.int32))
+
+
 @pytest.mark.parametrize("act", ["gelu_tanh", "swiglu", "situ", "geglu_erf", "gelu_erf"])
 def test_quantize_act(act):
     """Each fused input activation over three shapes (edge, C2-like, C5-like
@@ -469,6 +490,21 @@ def test_quantize_row_matches_the_reference_fixture():
     tie = torch.tensor([[127.0, 254.0, -254.0, 63.0] + [0.0] * 4], dtype=torch.bfloat16)
     q, _ = int8.quantize_row(tie.to(DEV))
     assert bits(q)[0, :4].tolist() == [64, 127, -127, 32]
+
+
+def test_quantize_row_reference_probe_rows():
+    """The rows of the reference's own probe of its Triton row quantizer
+    (triton/quantize.py:234-255): 64 x 3072 and 64 x 8192 of N(0, 0.4), and
+    the tie rows arange(-8, 8) / 2, bit-exact against the oracle."""
+    from xpu_kernels import int8
+    g = torch.Generator().manual_seed(0)
+    tie = (torch.arange(-8, 8, dtype=torch.float32) * 0.5).repeat(64, 1).to(torch.bfloat16)
+    for x in [(torch.randn(64, 3072, generator=g) * 0.4).to(torch.bfloat16),
+              (torch.randn(64, 8192, generator=g) * 0.4).to(torch.bfloat16), tie]:
+        q, s = int8.quantize_row(x.to(DEV))
+        qr, sr = O.quantize_row(bits(x))
+        assert np.array_equal(bits(q), qr)
+        assert np.array_equal(bits(s).view(np.uint32), sr.view(np.uint32))
 
 
 @pytest.mark.parametrize("m,k", [(64, 5120), (3, 24), (100, 1000), (40, 8192), (7, 8200)])

@@ -96,6 +96,23 @@ def test_gelu_tanh_and_geglu_within_a_few_values(G):
 
 # ------------------------------------------------------------------ known answers
 
+def test_geglu_reads_hidden_then_gate():
+    """The reference's half-order probe (debug/verify_ffn_geglu.py:116-127):
+    hidden = 1, gate = -2 must give bf16(1 * bf16(gelu(-2))), not
+    bf16(-2 * bf16(gelu(1))); the activated row is constant, and the rotation
+    (each radix-4 stage's rows sum to 2, scaled by 1/2) keeps a constant row
+    constant: every code is -127."""
+    m, k = 8, 256
+    x = np.zeros((m, 2 * k), np.float32)
+    x[:, :k], x[:, k:] = 1.0, -2.0
+    q, s = O.convrot_quantize(O.f32_to_bf16_bits(x), O.ACT_IDS["geglu_erf"])
+    y = O.bf16_bits_to_f32(O.f32_to_bf16_bits(O.activation(4, np.float32(1.0), np.float32(-2.0))))
+    assert -0.05 < float(y) < -0.04  # gelu(-2) = -0.0455; the swapped halves give -1.68
+    qr, sr = O.convrot_quantize(O.f32_to_bf16_bits(np.full((m, k), y, np.float32)))
+    assert np.array_equal(q, qr) and np.array_equal(s.view(np.uint32), sr.view(np.uint32))
+    assert (q == -127).all()
+
+
 def test_ties_round_to_even():
     # tests/test_quantize.py:84-91 of the reference
     q, s = O.quantize_row(np.array([[127.0, 254.0, -254.0, 63.0]], np.float32))
