@@ -235,9 +235,8 @@ FfnLayout ffn_layout(int64_t M, int64_t K, int64_t inner, int act) {
     size_t off = 0;
     L.xq = off; off += align256(static_cast<size_t>(M) * K);
     L.xs = off; off += align256(static_cast<size_t>(M) * 4);
-    L.mid = off;
-    if (act == 4) off += align256(static_cast<size_t>(M) * inner * 2);        // y bf16
-    else off += align256(static_cast<size_t>(M) * inner * (act == 5 ? 4 : 8));  // int32 acc
+    (void)act;  // every activation's intermediate is the bf16 y
+    L.mid = off; off += align256(static_cast<size_t>(M) * inner * 2);
     L.q2 = off; off += align256(static_cast<size_t>(M) * inner);
     L.xs2 = off; off += align256(static_cast<size_t>(M) * 4);
     L.total = off;
@@ -485,21 +484,15 @@ int xpuint8_ffn_stream(const void *stream, const void *x, const int8_t *up_w8,
     int8_t *q2 = reinterpret_cast<int8_t *>(ws + L.q2);
     float *xs2 = reinterpret_cast<float *>(ws + L.xs2);
     if (int rc = convrot_quantize(s, x, xq, xs, M, K, 0)) return rc;
-    if (activation == 4) {
-        void *y = ws + L.mid;
-        if (int rc = int_mm_common(s, kEpiGegluBf16, xq, up_w8, y, xs, up_scale, nullptr, M, inner,
-                                   K, 0, inner, true))
-            return rc;
-        if (int rc = convrot_quantize(s, y, q2, xs2, M, inner, 0)) return rc;
-    } else {
-        int32_t *acc = reinterpret_cast<int32_t *>(ws + L.mid);
-        const int64_t n_up = activation == 5 ? inner : 2 * inner;
-        if (int rc = int_mm_common(s, kEpiRawI32, xq, up_w8, acc, nullptr, nullptr, nullptr, M,
-                                   n_up, K, 0, n_up, true))
-            return rc;
-        if (int rc = dequant_act_quantize(s, acc, q2, xs2, xs, up_scale, M, inner, activation))
-            return rc;
-    }
+    // the up-projection's epilogue dequantizes, applies the activation and
+    // stores y bf16 [M, inner]; y's rotate+quantize is then the reference's
+    // dequant_act_quantize of the int32 accumulator (which rounds the dequant
+    // and the activation to bf16 at the same points)
+    void *y = ws + L.mid;
+    const int epi = activation == 4 ? kEpiGegluBf16 : (activation == 3 ? kEpiSituBf16 : kEpiGeluBf16);
+    if (int rc = int_mm_common(s, epi, xq, up_w8, y, xs, up_scale, nullptr, M, inner, K, 0, inner, true))
+        return rc;
+    if (int rc = convrot_quantize(s, y, q2, xs2, M, inner, 0)) return rc;
     return int_mm_common(s, kEpiDequantBf16, q2, down_w8, out, xs2, down_scale, down_bias, M, K,
                          inner, 0, K, true);
 }

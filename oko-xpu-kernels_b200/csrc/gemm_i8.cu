@@ -15,6 +15,8 @@
 //   geglu   B holds [hidden | gate] rows; a CTA loads hidden rows [n, n+128)
 //           and gate rows [N+n, N+n+128) into one 256-wide B tile, and writes
 //           y = bf16(h * bf16(gelu_erf(g))) with h, g the bf16-rounded dequants
+//   situ    the same tiles, y = MossImage's situ of h and g (act.cuh)
+//   gelu    the dequant epilogue, then y = bf16(gelu_erf(bf16(dequant)))
 //   split   the dequant epilogue with the output's columns cut into parts that
 //           land in separate buffers (q, k, v of one projection GEMM)
 //
@@ -50,6 +52,7 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "act.cuh"
 #include "common.cuh"
 #include "internal.h"
 
@@ -251,6 +254,29 @@ __device__ __forceinline__ void geglu32(const uint32_t (&rh)[32], const uint32_t
     }
 }
 
+// y = bf16(situ(h, g)) from the hidden and gate accumulators: h, g the
+// bf16-rounded dequants, then the gate's and the hidden half's factors
+// (act.cuh; the reference's situ_reg, src/xpuint8.cpp:142-160) multiplied
+__device__ __forceinline__ void situ32(const uint32_t (&rh)[32], const uint32_t (&rg)[32],
+                                       const float *wsh, const float *wsg, f2 xs2, float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        const float2 wh = *reinterpret_cast<const float2 *>(wsh + j);
+        const float2 wg = *reinterpret_cast<const float2 *>(wsg + j);
+        float h0, h1, g0, g1;
+        un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rh[j])),
+                     static_cast<float>(static_cast<int32_t>(rh[j + 1]))),
+                 mul2(mk2(wh.x, wh.y), xs2)), h0, h1);
+        un2(mul2(mk2(static_cast<float>(static_cast<int32_t>(rg[j])),
+                     static_cast<float>(static_cast<int32_t>(rg[j + 1]))),
+                 mul2(mk2(wg.x, wg.y), xs2)), g0, g1);
+        round_bf16x2(h0, h1);
+        round_bf16x2(g0, g1);
+        v[j] = __fmul_rn(piece_situ_gate(g0), piece_situ_hidden(h0));
+        v[j + 1] = __fmul_rn(piece_situ_gate(g1), piece_situ_hidden(h1));
+    }
+}
+
 // Drain this warp's share of one accumulator tile: 32 rows (its TMEM lane
 // quarter) x columns [c0, c1), 32 columns at a time.
 template <int EPI>
@@ -303,15 +329,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &a, const OutMaps &
             }
         } else {
             float v[32];
-            if constexpr (EPI == kEpiDequantBf16) {
+            if constexpr (EPI == kEpiDequantBf16 || EPI == kEpiGeluBf16) {
                 tmem_wait_ld(r);
                 dequant32(r, s_ws + c, s_b + c, xs2, bias, v);
+                if constexpr (EPI == kEpiGeluBf16) {
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) v[t] = piece_gelu_erf(round_bf16(v[t]));
+                }
             } else {
                 uint32_t rg[32];
                 tmem_ld32(taddr + 128 + c, rg);
                 tmem_wait_ld(r);
                 tmem_wait_ld(rg);
-                geglu32(r, rg, s_ws + c, s_ws + 128 + c, xs2, v);
+                if constexpr (EPI == kEpiSituBf16) situ32(r, rg, s_ws + c, s_ws + 128 + c, xs2, v);
+                else geglu32(r, rg, s_ws + c, s_ws + 128 + c, xs2, v);
             }
             stage_reserve(lane);
             const uint32_t buf = bufs + bsel * kStageBytes;
@@ -391,7 +422,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     // the previous kernel is the activation quantizer).
 
     const int num_tiles = args.num_m * args.num_n;
-    constexpr bool GEGLU = (EPI == kEpiGegluBf16);
+    // the paired epilogues: B tiles of 128 hidden + 128 gate rows
+    constexpr bool GEGLU = (EPI == kEpiGegluBf16 || EPI == kEpiSituBf16);
     const int BN_OUT = GEGLU ? 128 : args.bn;
     const int B_ROWS = GEGLU ? BN : args.bn;  // MMA N: rows of B per pair tile
     const int B_HALF = B_ROWS / 2;            // rows of B this CTA loads
@@ -722,9 +754,10 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
         set_error("N must be a multiple of 16");
         return 2;
     }
-    const bool geglu = c.epilogue == kEpiGegluBf16;
-    if (geglu && (c.a_mn || c.b_mn)) {
-        set_error("the GEGLU epilogue needs K-major operands");
+    // the paired epilogues (GEGLU, situ): B holds [hidden | gate] rows
+    const bool geglu = c.epilogue == kEpiGegluBf16 || c.epilogue == kEpiSituBf16;
+    if ((geglu || c.epilogue == kEpiGeluBf16) && (c.a_mn || c.b_mn)) {
+        set_error("the activation epilogues need K-major operands");
         return 2;
     }
     if (c.split_n > 0) {
@@ -847,6 +880,10 @@ int launch_gemm(cudaStream_t s, const GemmCall &c) {
             break;
         case kEpiGegluBf16:
             return launch_sized<kEpiGegluBf16, false, false>(s, ma, mb, mo, a, tiles);
+        case kEpiSituBf16:
+            return launch_sized<kEpiSituBf16, false, false>(s, ma, mb, mo, a, tiles);
+        case kEpiGeluBf16:
+            return launch_sized<kEpiGeluBf16, false, false>(s, ma, mb, mo, a, tiles);
         case kEpiDequantWide:
             if (!c.a_mn && !c.b_mn) return launch_sized<kEpiDequantWide, false, false>(s, ma, mb, mo, a, tiles);
             break;

@@ -45,7 +45,17 @@ int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t
 // kEpiDequantWide: the dequant epilogue storing 32 rows x 64 columns (128-byte
 // row segments) per TMA store instead of 32 x 32, one ring stage fewer: for
 // outputs written over NVLink, where small writes waste link bandwidth
-enum GemmEpilogue { kEpiRawI32 = 0, kEpiDequantBf16 = 1, kEpiGegluBf16 = 2, kEpiDequantWide = 3 };
+// kEpiSituBf16: the GEGLU tile layout ([hidden | gate] rows) with MossImage's
+// situ; kEpiGeluBf16: the dequant epilogue followed by the erf-GELU (each the
+// activation of the fused FFN's up-projection, stored as bf16)
+enum GemmEpilogue {
+    kEpiRawI32 = 0,
+    kEpiDequantBf16 = 1,
+    kEpiGegluBf16 = 2,
+    kEpiDequantWide = 3,
+    kEpiSituBf16 = 4,
+    kEpiGeluBf16 = 5
+};
 struct GemmCall {
     int epilogue = kEpiRawI32;
     const int8_t *a = nullptr;  // [M,K] (a_mn=0) or [K,M] (a_mn=1), row stride lda

@@ -651,6 +651,25 @@ def test_geglu_ffn_equals_the_unfused_chain():
     assert diff / fused.numel() < CODE_RATE
 
 
+@pytest.mark.parametrize("act", ["situ", "gelu_erf"])
+def test_ffn_equals_the_accumulator_chain(act):
+    """The fused FFN (the activation in the up-projection's epilogue, y stored
+    as bf16 and rotated + quantized) equals the reference's own structure run
+    on the GPU -- the int32 accumulator, dequant_act_quantize, the down GEMM
+    (ops.py:713-718) -- bit for bit, on a ragged row count."""
+    from xpu_kernels import int8
+    m, k, inner = 300, 1280, 1280
+    n_up = 2 * inner if act in int8.PAIRED_ACTIVATIONS else inner
+    x = rand_bf16((m, k), 185).to(DEV)
+    up8, up_s = int8.prepare_weight(rand_bf16((n_up, k), 186, scale=0.02).to(DEV))
+    dn8, dn_s = int8.prepare_weight(rand_bf16((k, inner), 187, scale=0.02).to(DEV))
+    fused = int8.ffn(x, up8, up_s, dn8, dn_s, act=act)
+    xq, xs = int8.quantize(x)
+    q2, xs2 = int8.dequant_act_quantize(int8.int_mm(xq, up8), xs, up_s, act)
+    chain = int8.dequant(int8.int_mm(q2, dn8), xs2, dn_s)
+    assert torch.equal(fused.view(torch.int16), chain.view(torch.int16))
+
+
 def test_selftest_passes():
     from xpu_kernels import int8
     from xpu_kernels.int8.selftest import run_checks
