@@ -133,16 +133,24 @@ constexpr int stage_bytes() { return EPI == kEpiDequantWide ? 32 * 128 : 32 * 64
 
 // Per-epilogue configuration.  The epilogue warps come in groups of four, one
 // per TMEM lane quarter (warp w reads lanes 32*(w%4)..+31), each group draining
-// its share of the tile's columns.  Two groups: a third or fourth group drains
-// the last tile sooner but costs a ring stage of shared memory and slows the
-// main loop more than it gains (measured at M=2048, N=10240, K=1280).  The ring
-// takes what shared memory the staging buffers leave (227 KB per CTA).
+// its share of the tile's columns.  Two groups for the dequant epilogues: a
+// third or fourth group drains the last tile sooner but costs a ring stage of
+// shared memory and slows the main loop more than it gains (measured at
+// M=2048, N=10240, K=1280).  Four groups for the activation epilogues, whose
+// drain is the slower side.  The ring takes what shared memory the staging
+// buffers leave (227 KB per CTA).
+#ifndef XPU_ACT_EPI_WARPS
+#define XPU_ACT_EPI_WARPS 16
+#endif
 template <int EPI>
 struct Cfg {
-    static constexpr int kEpiWarps = 8;
+    // the activation epilogues evaluate a transcendental per output, so their
+    // drain is slower than the main loop: more warps drain each tile
+    static constexpr bool kHeavy = EPI == kEpiSituBf16 || EPI == kEpiGeluBf16 || EPI == kEpiGegluBf16;
+    static constexpr int kEpiWarps = kHeavy ? XPU_ACT_EPI_WARPS : 8;
     static constexpr int kGroups = kEpiWarps / 4;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
-    static constexpr int kStages = EPI == kEpiDequantWide ? 5 : 6;
+    static constexpr int kStages = (EPI == kEpiDequantWide || (kHeavy && kEpiWarps > 8)) ? 5 : 6;
     static constexpr int kEpiSmem = kEpiWarps * kStageBufs * stage_bytes<EPI>();
     static constexpr size_t kSmemBytes =
         static_cast<size_t>(kStages) * STAGE_BYTES + kEpiSmem + 2 * BN * 4 + 256;
@@ -537,9 +545,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
         // ---------------------------------------------------------- epilogue (both CTAs)
         const int quarter = warp & 3;         // TMEM lanes 32*quarter .. +31
         const int group = (warp - 2) >> 2;    // which share of the tile's columns
-        // GEGLU: 64 output columns per group; otherwise BN / groups columns of
+        // paired: 128 / groups output columns per group; otherwise BN / groups columns of
         // the accumulator per group, clipped to the tile's bn
-        constexpr int kCols = GEGLU ? 64 : BN / Cfg<EPI>::kGroups;
+        constexpr int kCols = GEGLU ? 128 / Cfg<EPI>::kGroups : BN / Cfg<EPI>::kGroups;
         const int col0 = kCols * group;
         const int col1 = GEGLU ? col0 + kCols : min(col0 + kCols, args.bn);
         const int et = threadIdx.x - 64;      // index among the epilogue threads; the
