@@ -35,7 +35,10 @@ Also reported on the same line:
   copied from pinned host memory and the bf16 result copied back each step;
 * ``cpu_baseline``: the reference's own CPU path (reference/convrot_linear.py's
   op sequence with torch._int_mm, the Hadamard in place of its identity
-  placeholder), restated in oracle/convrot_torch_cpu.py, on the full workload.
+  placeholder), restated in oracle/convrot_torch_cpu.py, on the full workload;
+* ``other_configs`` (one GPU): the other BASELINE configs through the public
+  API, device time per call from CUDA graphs -- C1 and one C2 linear, the C3
+  GEGLU FFN, C4's int8 dx and dW.
 
 ``--impl reference`` times that same CPU path on the host cores (the
 reference's device library is SYCL for Intel GPUs and does not build here) on
@@ -436,6 +439,9 @@ def run_gpu(args):
     if rank == 0:
         result.update(_rank0_extras(args, lib, L, dev, sets, stream))
     del sets
+    if rank == 0 and ws == 1:
+        torch.cuda.empty_cache()
+        result["other_configs"] = _other_configs(dev)
     torch.cuda.empty_cache()
     # config C5 at N ranks: M-sharded (every rank), then the N-sharded all-gather
     result["c5_mshard"] = _c5_mshard(args, dev, stream, ws, rank)
@@ -547,6 +553,71 @@ def _c5_nshard(args, dev, stream, ws, rank):
             "forms_bit_identical": same,
             "output_bytes_sent_per_rank": m * (n // ws) * 2 * (ws - 1),
             "shape": f"x bf16 [{m},{C5_K}] on every rank, W [{n},{C5_K}] split over {ws} ranks"}
+
+
+def _graph_us(fn, n, reps=5):
+    """Device time per call (us) of n calls captured in one CUDA graph, the
+    graph replayed `reps` times between CUDA events (after eager warm-up)."""
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for i in range(n):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * n)
+    del graph
+    return us
+
+
+def _other_configs(dev):
+    """The other BASELINE configs on one GPU through the public API (device
+    time per call from CUDA graphs, warm, two rotating input sets; synthetic
+    seeded inputs of the configs' shapes and distributions): C1 linear, one
+    C2 projection, the C3 GEGLU FFN, and C4's int8 dx and dW."""
+    import xpu_kernels as xk
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def bf(*shape, s=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * s).to(torch.bfloat16)
+
+    out = {}
+    for name, (m, k, n) in {"C1_linear": (256, 1024, 1024), "C2_linear": (2048, 1280, 1280)}.items():
+        xs_ = [bf(m, k) for _ in range(2)]
+        w8, wsc = xk.prepare_weight(bf(n, k, s=0.02))
+        b = bf(n, s=0.01).float()
+        us = _graph_us(lambda i: xk.linear(xs_[i % 2], w8, wsc, b), 20)
+        out[name] = {"us": us, "tops": 2.0 * m * n * k / (us * 1e-6) / 1e12, "shape": [m, k, n]}
+    m, k, inner = 2048, 1280, 5120
+    xs_ = [bf(m, k) for _ in range(2)]
+    up8, ups = xk.prepare_weight(bf(2 * inner, k, s=0.02))
+    dn8, dns = xk.prepare_weight(bf(k, inner, s=0.02))
+    us = _graph_us(lambda i: xk.ffn(xs_[i % 2], up8, ups, dn8, dns, act="geglu_erf"), 10)
+    out["C3_ffn_geglu"] = {"us": us, "tops": (2.0 * m * 2 * inner * k + 2.0 * m * k * inner) / (us * 1e-6) / 1e12,
+                           "shape": [m, k, inner]}
+    m, k, n = 4096, 1280, 5120
+    w8, wsc = xk.prepare_weight(bf(n, k, s=0.02))
+    dys = [bf(m, n, s=1e-3) for _ in range(2)]
+    xq, xsc = xk.quantize(bf(m, k))
+    us = _graph_us(lambda i: xk.linear_dx_int8(dys[i % 2], w8, wsc), 10)
+    out["C4_dx_int8"] = {"us": us, "tops": 2.0 * m * n * k / (us * 1e-6) / 1e12, "shape": [m, k, n]}
+    us = _graph_us(lambda i: xk.linear_dw_int8(dys[i % 2], xq, xsc), 10)
+    out["C4_dw_int8"] = {"us": us, "tops": 2.0 * m * n * k / (us * 1e-6) / 1e12, "shape": [m, k, n]}
+    out["timing"] = ("device time per call: calls captured in a CUDA graph, replayed between CUDA "
+                     "events, two rotating input sets; shapes [M, K, N] (C3: [M, K, inner])")
+    return out
 
 
 def _time_launches(fn, n, stream):
