@@ -44,10 +44,19 @@ __device__ __forceinline__ uint32_t q_div(float x, float s, float y) {
 // packed operation rounds as the scalar one): the two codes in the low bytes
 // of the halves.  The final add is an FMA with a unit product, because ptxas
 // contracts a packed multiply feeding a packed add into one rounding.
-__device__ __forceinline__ f2 q_div2(f2 x, f2 s, f2 y) {
+// ns = -s, so that the exact remainder x - s q0 is one FMA.
+__device__ __forceinline__ f2 q_div2(f2 x, f2 ns, f2 y) {
     const f2 q0 = mul2(x, y);
-    const f2 r = fma2(f2{q0.v ^ 0x8000000080000000ull}, s, x);  // x - s q0, exact
+    const f2 r = fma2(q0, ns, x);  // x - s q0, exact
     return fma2(fma2(r, y, q0), mk2(1.0f, 1.0f), mk2(12582912.0f, 12582912.0f));
+}
+
+// the low bytes of four words (the codes q_div / q_div2 leave there) as one
+// word, c0 in the lowest byte: three byte permutes
+__device__ __forceinline__ uint32_t pack_codes4(float c0, float c1, float c2, float c3) {
+    const uint32_t lo = __byte_perm(__float_as_uint(c0), __float_as_uint(c1), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(c2), __float_as_uint(c3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 
 template <bool COLSCALE>
@@ -186,22 +195,18 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
         const float y = row_scale_inv(rm, s);
         if (t == 0) scale[row] = s;
         int8_t *qr = q + row * K;
-        const f2 s2 = mk2(s, s), y2 = mk2(y, y);
+        const f2 ns2 = mk2(-s, -s), y2 = mk2(y, y);
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             const int ch = t + 128 * c;
             if (ch < nch) {
-                uint32_t b[8];
+                float b[8];
 #pragma unroll
-                for (int j = 0; j < 8; j += 2) {
-                    float c0, c1;
-                    un2(q_div2(mk2(v[8 * c + j], v[8 * c + j + 1]), s2, y2), c0, c1);
-                    b[j] = __float_as_uint(c0) & 0xFFu;
-                    b[j + 1] = __float_as_uint(c1) & 0xFFu;
-                }
+                for (int j = 0; j < 8; j += 2)
+                    un2(q_div2(mk2(v[8 * c + j], v[8 * c + j + 1]), ns2, y2), b[j], b[j + 1]);
                 uint2 o;
-                o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
-                o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+                o.x = pack_codes4(b[0], b[1], b[2], b[3]);
+                o.y = pack_codes4(b[4], b[5], b[6], b[7]);
                 __stcs(reinterpret_cast<uint2 *>(qr + 8 * ch), o);
             }
         }
@@ -215,14 +220,16 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
 constexpr int kColW = 512;     // columns per tile
 constexpr int kColLanes = 8;   // rows read at once (one per warp)
 
-// the 16 fp32 values g = dy * x of a lane's 16 columns of one row, as 8 pairs
-__device__ __forceinline__ void load_g16(const uint16_t *p, float x, f2 (&g)[8]) {
-    const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p));
-    const uint4 b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
+// the 16 fp32 values g = dy * x of a lane's 16 columns of one row, as 8
+// pairs, from the row's 32 bytes (a, b)
+__device__ __forceinline__ void g16(uint4 a, uint4 b, float x, f2 (&g)[8]) {
     const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     const f2 x2 = mk2(x, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) g[j] = mul2(mk2(bf16_lo(u[j]), bf16_hi(u[j])), x2);
+}
+__device__ __forceinline__ void load_g16(const uint16_t *p, float x, f2 (&g)[8]) {
+    g16(__ldcg(reinterpret_cast<const uint4 *>(p)), __ldcg(reinterpret_cast<const uint4 *>(p) + 1), x, g);
 }
 
 // Pass 1: column abs-maxima of g = dy * xs over a run of rows, reduced over
@@ -291,16 +298,36 @@ __global__ void colscale_kernel(float *tg, int64_t N) {
 // per lane and row in one 16-byte store.  FROM_AMAX: the CTA makes the scales
 // of its 512 columns from the column maxima of pass 1 (amax; the CTAs of the
 // first run also write them to tg); otherwise it reads them from tg.  Each
-// column's reciprocal is made once per CTA.
+// column's reciprocal is made once per CTA, and the first four rows of each
+// lane are loaded before that, so that their latency covers it.
 template <bool FROM_AMAX>
-__global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restrict__ dy,
+__global__ void __launch_bounds__(256, 3) colquant_kernel(const uint16_t *__restrict__ dy,
                                                        const float *__restrict__ xs,
                                                        const unsigned int *__restrict__ amax,
                                                        float *__restrict__ tg, int8_t *__restrict__ gq,
                                                        int64_t M, int64_t N, int64_t rows) {
+    constexpr int kAhead = 4;
     __shared__ float s_t[kColW], s_y[kColW];
     pdl_wait();
     pdl_trigger();
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * kColW + 16 * l;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * rows;
+    const int64_t m1 = min(M, m0 + rows);
+    uint4 pa[kAhead], pb[kAhead];
+    float px[kAhead];
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) {
+        const int64_t m = m0 + w + kColLanes * i;
+        pa[i] = pb[i] = make_uint4(0u, 0u, 0u, 0u);
+        px[i] = 0.f;
+        if (n < N && m < m1) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(dy + m * N + n);
+            pa[i] = __ldcg(p);
+            pb[i] = __ldcg(p + 1);
+            px[i] = __ldg(xs + m);
+        }
+    }
 #pragma unroll
     for (int h = 0; h < kColW / 256; ++h) {
         const int c = threadIdx.x + 256 * h;
@@ -319,23 +346,16 @@ __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restric
         s_y[c] = y;
     }
     __syncthreads();
-    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t n = static_cast<int64_t>(blockIdx.x) * kColW + 16 * l;
     if (n >= N) return;
-    f2 t2[8], y2[8];
+    f2 nt2[8], y2[8];  // -t (the remainder below is one FMA) and RN(1 / t), in pairs
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        t2[j] = mk2(s_t[16 * l + 2 * j], s_t[16 * l + 2 * j + 1]);
+        nt2[j] = mk2(-s_t[16 * l + 2 * j], -s_t[16 * l + 2 * j + 1]);
         y2[j] = mk2(s_y[16 * l + 2 * j], s_y[16 * l + 2 * j + 1]);
     }
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * rows;
-    const int64_t m1 = min(M, m0 + rows);
     const f2 one = mk2(1.0f, 1.0f), magic = mk2(12582912.0f, 12582912.0f);
-#pragma unroll 4
-    for (int64_t m = m0 + w; m < m1; m += kColLanes) {
-        f2 g[8];
-        load_g16(dy + m * N + n, __ldg(xs + m), g);
-        uint32_t b[16];
+    auto quant_row = [&](int64_t m, const f2 (&g)[8]) {
+        float c[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             // RN(g / t) by Markstein's correction of RN(g * y), then
@@ -343,19 +363,30 @@ __global__ void __launch_bounds__(256) colquant_kernel(const uint16_t *__restric
             // FMA with a unit product: a packed multiply feeding a packed add
             // would be contracted into one rounding)
             const f2 q0 = mul2(g[j], y2[j]);
-            const f2 r = fma2(f2{q0.v ^ 0x8000000080000000ull}, t2[j], g[j]);  // -q0 * t + g
-            const f2 q = fma2(fma2(r, y2[j], q0), one, magic);
-            float c0, c1;
-            un2(q, c0, c1);
-            b[2 * j] = __float_as_uint(c0) & 0xFFu;
-            b[2 * j + 1] = __float_as_uint(c1) & 0xFFu;
+            const f2 r = fma2(q0, nt2[j], g[j]);  // g - q0 * t, exact
+            un2(fma2(fma2(r, y2[j], q0), one, magic), c[2 * j], c[2 * j + 1]);
         }
         uint4 o;
-        o.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
-        o.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
-        o.z = b[8] | (b[9] << 8) | (b[10] << 16) | (b[11] << 24);
-        o.w = b[12] | (b[13] << 8) | (b[14] << 16) | (b[15] << 24);
+        o.x = pack_codes4(c[0], c[1], c[2], c[3]);
+        o.y = pack_codes4(c[4], c[5], c[6], c[7]);
+        o.z = pack_codes4(c[8], c[9], c[10], c[11]);
+        o.w = pack_codes4(c[12], c[13], c[14], c[15]);
         __stcs(reinterpret_cast<uint4 *>(gq + m * N + n), o);
+    };
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) {
+        const int64_t m = m0 + w + kColLanes * i;
+        if (m < m1) {
+            f2 g[8];
+            g16(pa[i], pb[i], px[i], g);
+            quant_row(m, g);
+        }
+    }
+#pragma unroll 4
+    for (int64_t m = m0 + w + kColLanes * kAhead; m < m1; m += kColLanes) {
+        f2 g[8];
+        load_g16(dy + m * N + n, __ldg(xs + m), g);
+        quant_row(m, g);
     }
 }
 
