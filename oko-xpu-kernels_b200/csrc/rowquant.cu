@@ -12,10 +12,10 @@
 //
 // colquant: the operand of the int8 weight gradient.  g[m,n] = dy[m,n]*xs[m]
 //   (fp32), per-column tg[n] = max(amax_m |g| / 127, 1e-30),
-//   gq[m,n] = clamp(rint(g / tg[n]), +-127).  Three launches over tiles of
-//   128 rows x 256 columns: column abs-max (reduced per tile in shared memory,
-//   then one atomicMax per column on the bit pattern of a non-negative
-//   float), scale, quantize.
+//   gq[m,n] = clamp(rint(g / tg[n]), +-127).  Launches over tiles of 512
+//   columns x a run of rows: zero the maxima, column abs-max (reduced per
+//   tile in shared memory, then one atomicMax per column on the bit pattern
+//   of a non-negative float), scale (unless pass 2 makes them), quantize.
 //
 // Division.  Every x / s is RN(x / s) computed as Markstein's correction of
 // the product with the correctly rounded reciprocal y = RN(1 / s) (Markstein,
@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(256) quantize_row_kernel(const uint16_t *__res
                                                            int8_t *__restrict__ q,
                                                            float *__restrict__ scale, int64_t K) {
     __shared__ float red[8];
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const uint16_t *xr = x + row * K;
     int8_t *qr = q + row * K;
@@ -137,6 +139,8 @@ __global__ void __launch_bounds__(128) quantize_row_reg_kernel(const uint16_t *_
                                                                float *__restrict__ scale,
                                                                int64_t M, int64_t K) {
     __shared__ float red[2][4];
+    pdl_wait();
+    pdl_trigger();  // the consumer (a GEMM) may set up while the rows are quantized
     const int t = threadIdx.x;
     const int nch = static_cast<int>(K >> 3);
     uint32_t csb[COLSCALE ? CH * 4 : 1];  // bf16(col_scale) of this thread's columns, in pairs
@@ -280,6 +284,15 @@ __global__ void __launch_bounds__(256) colamax_kernel(const uint16_t *__restrict
             atomicMax(amax + col, __float_as_uint(v));
         }
     }
+}
+
+// the column maxima zeroed before pass 1 (a kernel rather than a memset node,
+// so that pass 1 may launch while it runs)
+__global__ void colzero_kernel(unsigned int *amax, int64_t N) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (n < N) amax[n] = 0u;
 }
 
 // tg[n] = max(amax[n] / 127, 1e-30) in place (after the atomic form of pass 1)
@@ -430,12 +443,23 @@ int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, i
     const uint16_t *xb = static_cast<const uint16_t *>(x);
     const int64_t nch = K / 8;
     const int ch = static_cast<int>((nch + 127) / 128);
+    // programmatic serialization: the kernels wait for the one before them
+    // before their first global access, and let the next one launch at once
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (ch <= 8) {
         // persistent CTAs: as many as are resident at once, at most one per row
         auto go = [&](auto kern, const float *c) {
             const int per = resident_per_sm(kern, 128);
             const int64_t grid = std::min<int64_t>(M, static_cast<int64_t>(num_sms()) * per);
-            kern<<<static_cast<unsigned>(grid), 128, 0, s>>>(xb, c, q, scale, M, K);
+            cfg.gridDim = dim3(static_cast<unsigned>(grid));
+            cfg.blockDim = dim3(128);
+            cudaLaunchKernelEx(&cfg, kern, xb, c, q, scale, M, K);
         };
 #define XPU_RQ_CASE(C)                                                     \
     case C:                                                                \
@@ -456,10 +480,12 @@ int launch_quantize_row(cudaStream_t s, const void *x, const float *col_scale, i
 #undef XPU_RQ_CASE
         return launch_status("quantize_row");
     }
+    cfg.gridDim = dim3(static_cast<unsigned>(M));
+    cfg.blockDim = dim3(256);
     if (col_scale)
-        quantize_row_kernel<true><<<static_cast<unsigned>(M), 256, 0, s>>>(xb, col_scale, q, scale, K);
+        cudaLaunchKernelEx(&cfg, quantize_row_kernel<true>, xb, col_scale, q, scale, K);
     else
-        quantize_row_kernel<false><<<static_cast<unsigned>(M), 256, 0, s>>>(xb, nullptr, q, scale, K);
+        cudaLaunchKernelEx(&cfg, quantize_row_kernel<false>, xb, static_cast<const float *>(nullptr), q, scale, K);
     return launch_status("quantize_row");
 }
 
@@ -484,8 +510,6 @@ int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t
         return 2;
     }
     unsigned int *amax = amax_ws ? amax_ws : reinterpret_cast<unsigned int *>(tg);
-    if (cudaMemsetAsync(amax, 0, static_cast<size_t>(N) * sizeof(float), s) != cudaSuccess)
-        return launch_status("colquant memset");
     // the kernels launch with programmatic serialization (each waits for the
     // one before it before touching memory)
     cudaLaunchAttribute attr[1];
@@ -496,6 +520,9 @@ int launch_colquant(cudaStream_t s, const void *dy, const float *x_scale, int8_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3(static_cast<unsigned>((N + 255) / 256));
+    if (cudaLaunchKernelEx(&cfg, colzero_kernel, amax, N) != cudaSuccess)
+        return launch_status("colquant (zero the maxima)");
     cfg.gridDim = dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(runs_a));
     if (cudaLaunchKernelEx(&cfg, colamax_kernel, d, x_scale, amax, M, N, rows_a) != cudaSuccess)
         return launch_status("colquant (column maxima)");
