@@ -91,6 +91,8 @@ def main(argv=None):
     ap.add_argument("--K", type=int, default=1280)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--sets", type=int, default=2)
+    ap.add_argument("--colscale", action="store_true",
+                    help="quantize_row: with a column scale (the form linear_dx_int8 runs)")
     ap.add_argument("--act", type=int, default=4,
                     help="dequant_act / ffn: 3 situ, 4 GEGLU (paired), 5 GELU-erf (unpaired)")
     a = ap.parse_args(argv)
@@ -141,6 +143,9 @@ def main(argv=None):
         Q = [torch.empty(M, K, dtype=torch.bfloat16 if a.case == "rotate" else torch.int8,
                          device=dev) for _ in range(S)]
         sc = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(S)]
+        # --colscale: the column-scaled form linear_dx_int8 runs (x * bf16(col_scale))
+        cs = f32(K) if a.colscale else None
+        cs_ptr = _ptr(cs) if a.colscale else None
 
         def fn(i):
             j = i % S
@@ -149,7 +154,7 @@ def main(argv=None):
             elif a.case == "rotate":
                 rc = lib.xpuint8_convrot_rotate_bf16_stream(_stream(dev), _ptr(X[j]), _ptr(Q[j]), M, K)
             else:
-                rc = lib.xpuint8_quantize_row_stream(_stream(dev), _ptr(X[j]), None, _ptr(Q[j]), _ptr(sc[j]), M, K)
+                rc = lib.xpuint8_quantize_row_stream(_stream(dev), _ptr(X[j]), cs_ptr, _ptr(Q[j]), _ptr(sc[j]), M, K)
             assert rc == 0, lib.xpuint8_last_error()
         nbytes = (4 * M * K) if a.case == "rotate" else (3 * M * K + 4 * M)
         t = _time(fn, a.iters, st)
